@@ -1,0 +1,141 @@
+// sb_device.cuh -- device-side building blocks of the B200 Stratego simulator.
+//
+// One warp owns one env at a time.  The env's 256-byte record is staged in
+// shared memory, the 100 squares are spread over the 32 lanes (square
+// lane + 32k), and everything that is per-env scalar (validating and applying
+// the action, the trackers) runs warp-uniformly: every lane computes the same
+// values from shared memory and lane 0 stores them.
+//
+// Board square code (1 byte per square, packed 10x10):
+//   bits 0-3 piece type (0 none, 1 Spy .. 10 Marshal, 11 Flag, 12 Bomb)
+//   bit  4   owner is Blue (only meaningful when bit 5 is set)
+//   bit  5   occupied
+//   bit  6   moved flag of the square   (csrc/stratego_buffer.cu:243-253)
+//   bit  7   revealed flag of the square
+// Empty squares keep bits 0-5 clear; bits 6-7 are per-square tracker flags
+// that survive the piece leaving, as in the reference's bool[100] tensors.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sb {
+
+constexpr int NSQ = 100;
+constexpr int NACT = 10000;
+constexpr int NHIST = 32;
+constexpr int NRING = 64;
+constexpr int NCH = 488;
+constexpr int REC = 256;
+constexpr unsigned FULL = 0xffffffffu;
+
+// Record layout (byte offsets).  Every field is naturally aligned.
+constexpr int R_BOARD = 0;      // u8[100]
+constexpr int R_PLAYER = 100;   // i8  side to move (0 Red, 1 Blue)
+constexpr int R_OUTCOME = 101;  // i8  -1 ongoing, 0 red win, 1 blue win, 2 draw
+constexpr int R_TERM = 102;     // u8
+constexpr int R_FLAGCAP = 103;  // u8
+constexpr int R_MOVENUM = 104;  // i32
+constexpr int R_MSA = 108;      // i32 moves since last attack
+constexpr int R_TSINCE = 112;   // i32 terminated_since
+constexpr int R_HHEAD = 116;    // u8  history ring head
+constexpr int R_HLEN = 117;     // u8  history ring length
+constexpr int R_TSVIOL = 118;   // u8  two-square violation (sticky)
+constexpr int R_CHVIOL = 119;   // u8  chasing violation (sticky)
+constexpr int R_TSCOUNT = 120;  // i32[2]
+constexpr int R_TSLO = 128;     // i16[2]
+constexpr int R_TSHI = 132;     // i16[2]
+constexpr int R_CHHEAD = 136;   // u8[2]
+constexpr int R_CHLEN = 138;    // u8[2]
+constexpr int R_CHLAST = 140;   // i8[2]
+constexpr int R_PROP = 142;     // i16 cached proposal (-1 none)
+constexpr int R_ZHASH = 144;    // i64 Zobrist hash of the board
+constexpr int R_EPISODE = 152;  // i32 pool resets done in this env
+constexpr int R_INVALID = 156;  // i32 rejected actions
+constexpr int R_PROPPLY = 160;  // i32 ply the cached proposal was drawn for (-1 stale)
+constexpr int R_NLEGAL = 164;   // i16 legal moves of the side to move (with the proposal)
+constexpr int R_PROPKIND = 166; // u8  policy the cached proposal was drawn with
+constexpr int R_PROPLP = 168;   // f32 log-prob of the cached proposal
+constexpr int R_HIST = 176;     // i16[32] move-history ring
+
+constexpr uint8_t C_PIECE = 15, C_BLUE = 16, C_OCC = 32, C_MOVED = 64, C_REV = 128;
+
+enum : uint32_t {
+    TAG_SETUP = 1,
+    TAG_RESET = 2,
+    TAG_ACTION = 3,
+    TAG_LOGIT = 4,
+    TAG_BELIEF = 6,
+};
+
+template <typename T>
+__device__ __forceinline__ T& fld(uint8_t* rec, int off) {
+    return *reinterpret_cast<T*>(rec + off);
+}
+template <typename T>
+__device__ __forceinline__ const T& fld(const uint8_t* rec, int off) {
+    return *reinterpret_cast<const T*>(rec + off);
+}
+
+// Lakes: rows 4-5, columns 2, 3, 6, 7 (stratego/constants.py:25-28).
+__device__ __forceinline__ bool is_lake(int sq) {
+    return sq >= 40 && sq < 60 && ((0xCCu >> (sq % 10)) & 1u);
+}
+__device__ __forceinline__ bool can_move(int pt) { return pt >= 1 && pt <= 10; }
+__device__ __forceinline__ int owner_of(uint8_t c) { return (c & C_OCC) ? ((c >> 4) & 1) : -1; }
+
+__device__ __forceinline__ uint64_t zob(const int64_t* z, int sq, int owner, int piece) {
+    return (uint64_t)__ldg(z + (sq * 2 + owner) * 13 + piece);
+}
+
+// Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11).
+__device__ __forceinline__ uint4 philox(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint64_t seed) {
+    uint32_t k0 = (uint32_t)seed, k1 = (uint32_t)(seed >> 32);
+#pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        uint32_t hi0 = __umulhi(0xD2511F53u, c0), lo0 = 0xD2511F53u * c0;
+        uint32_t hi1 = __umulhi(0xCD9E8D57u, c2), lo1 = 0xCD9E8D57u * c2;
+        uint32_t n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
+        c0 = n0; c1 = lo1; c2 = n2; c3 = lo0;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+    return make_uint4(c0, c1, c2, c3);
+}
+
+__device__ __forceinline__ uint32_t mulshift(uint32_t u, uint32_t n) {
+    return (uint32_t)(((uint64_t)u * (uint64_t)n) >> 32);
+}
+
+__device__ __forceinline__ float u01(uint32_t w) {
+    return ((float)(w >> 8) + 0.5f) * (1.0f / 16777216.0f);
+}
+
+__device__ __forceinline__ uint64_t warp_xor64(uint64_t v) {
+    uint32_t lo = (uint32_t)v, hi = (uint32_t)(v >> 32);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        lo ^= __shfl_xor_sync(FULL, lo, o);
+        hi ^= __shfl_xor_sync(FULL, hi, o);
+    }
+    return ((uint64_t)hi << 32) | lo;
+}
+
+__device__ __forceinline__ int warp_sum(int v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+    return v;
+}
+
+// ---- bulk async copies shared -> global (TMA engine, no multicast) --------
+__device__ __forceinline__ void bulk_s2g(void* gdst, const void* ssrc, uint32_t bytes) {
+    uint32_t s = (uint32_t)__cvta_generic_to_shared(ssrc);
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(s), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+}  // namespace sb

@@ -1,0 +1,1266 @@
+// sb_kernels.cu -- B200 kernels and C ABI of the Stratego rollout simulator.
+//
+// The hot path is env_kernel<T>: one warp per env, one launch per ply, doing
+// (optionally) action sampling, move validation / combat / trackers /
+// terminal check, auto-reset from the setup pool, and the observation
+// outputs of the new state (legal mask, 488-channel infostate) in a single
+// pass over the env's 256-byte record.  Observations are staged in shared
+// memory and leave the SM as bulk asynchronous copies
+// (cp.async.bulk.global.shared::cta, the TMA engine, no multicast), so that
+// HBM sees long contiguous writes while the warp moves on.
+//
+// Semantics follow the reference simulator csrc/stratego_buffer.cu (cited per
+// function) with the Zobrist hash kept incrementally in the record instead of
+// being recomputed over 100 squares.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "sb_device.cuh"
+#include "stratego_b200.h"
+
+namespace sb {
+
+enum : uint32_t {
+    F_RESET_PLANES = 1u << 0,  // reset from setup planes (reference reset_terminated)
+    F_RESET_POOL = 1u << 1,    // reset from the setup pool
+    F_FORCE = 1u << 2,         // reset every env, not only terminated ones
+    F_APPLY = 1u << 3,         // apply one action per env
+    F_STEP = 1u << 4,          // step() semantics: stuck rule, transition outputs
+    F_AUTO_RESET = 1u << 5,    // after apply, reset terminated envs from the pool
+    F_PROPOSE = 1u << 6,       // cache a proposal for the new state at propose_ply
+    F_MASK_U8 = 1u << 7,
+    F_MASK_BITS = 1u << 8,
+    F_INFO = 1u << 9,
+    F_HAS_LEGAL = 1u << 10,
+    F_HASH = 1u << 11,
+    F_SAMPLE_OUT = 1u << 12,   // write the sampled action of the current state
+};
+
+struct KArgs {
+    uint8_t* rec;
+    int64_t* ring;
+    const int64_t* zob;
+    const uint8_t* pool;
+    int64_t pool_size;
+    int64_t n;
+    int64_t env_base;
+    uint64_t seed;
+    int32_t no_attack_limit, max_len, ts_limit, policy;
+    int32_t* status;
+    const float* logits;
+    uint32_t flags;
+    int32_t info_layout;
+    const int64_t* actions;
+    int64_t ply;
+    int64_t propose_ply;
+    const int8_t* setup_red;
+    const int8_t* setup_blue;
+    uint8_t* mask_u8;
+    uint8_t* mask_bits;
+    void* info;
+    float* reward;
+    uint8_t* done;
+    int64_t* action_taken;
+    float* logprob_taken;
+    int16_t* next_action;
+    float* next_logprob;
+    int64_t* hash;
+    uint8_t* has_legal;
+    int64_t* stats;
+    int64_t* sampled;
+    float* sampled_lp;
+    int32_t sm_warp, sm_r1, sm_hist, sm_mask, sm_bits;
+};
+
+constexpr int WARPS = 4;  // warps (envs in flight) per CTA
+constexpr int SM_RAYS = 256;
+constexpr int SM_PAT_OPP = 512;
+constexpr int SM_PAT_OWN = 912;
+constexpr int SM_FIXED = 1312;
+
+// ---------------------------------------------------------------------------
+// Legal moves
+// ---------------------------------------------------------------------------
+
+// Squares reachable from sq along `step` (at most maxs squares) for player p;
+// a scout slides until blocked, stopping on the first enemy
+// (csrc/stratego_buffer.cu:482-505).
+__device__ __forceinline__ int ray_len(const uint8_t* b, int sq, int step, int maxs, int p, bool scout) {
+    int len = 0;
+    for (int i = 0; i < maxs; ++i) {
+        sq += step;
+        if (is_lake(sq)) break;
+        const uint8_t c = b[sq];
+        if (c & C_OCC) {
+            if (((c >> 4) & 1) != p) ++len;
+            break;
+        }
+        ++len;
+        if (!scout) break;
+    }
+    return len;
+}
+
+// Ray lengths of every lane square for side p, packed as up | left<<4 |
+// right<<8 | down<<12 (the groups in ascending destination order), and the
+// per-square counts (csrc/stratego_buffer.cu:467-506).
+__device__ __forceinline__ void enumerate(const uint8_t* b, int p, uint16_t* rays, int lane, int cnt[4]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int sq = lane + 32 * k;
+        cnt[k] = 0;
+        if (sq < NSQ) {
+            const uint8_t c = b[sq];
+            const int pc = c & C_PIECE;
+            uint16_t packed = 0;
+            if ((c & C_OCC) && ((c >> 4) & 1) == p && can_move(pc)) {
+                const bool scout = pc == 2;
+                const int r = sq / 10, col = sq % 10;
+                const int up = ray_len(b, sq, -10, r, p, scout);
+                const int left = ray_len(b, sq, -1, col, p, scout);
+                const int right = ray_len(b, sq, 1, 9 - col, p, scout);
+                const int down = ray_len(b, sq, 10, 9 - r, p, scout);
+                packed = (uint16_t)(up | (left << 4) | (right << 8) | (down << 12));
+                cnt[k] = up + left + right + down;
+            }
+            rays[sq] = packed;
+        }
+    }
+    __syncwarp();
+}
+
+// j-th destination (0-based, ascending) of a packed ray set.
+__device__ __forceinline__ int decode_ray(int sq, uint32_t r, int j) {
+    const int up = r & 15, left = (r >> 4) & 15, right = (r >> 8) & 15;
+    if (j < up) return sq - 10 * (up - j);
+    j -= up;
+    if (j < left) return sq - (left - j);
+    j -= left;
+    if (j < right) return sq + 1 + j;
+    j -= right;
+    return sq + 10 * (1 + j);
+}
+
+// kth legal action in ascending src*100+dst order (warp-uniform result).
+__device__ int kth_action(int kth, const int cnt[4], const uint16_t* rays, int lane) {
+    int base = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int c = cnt[k];
+        int incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(FULL, incl, o);
+            if (lane >= o) incl += v;
+        }
+        const int total = __shfl_sync(FULL, incl, 31);
+        if (kth < base + total) {
+            const unsigned m = __ballot_sync(FULL, kth < base + incl);
+            const int L = __ffs(m) - 1;
+            const int excl = __shfl_sync(FULL, incl - c, L);
+            const int sq = L + 32 * k;
+            return sq * 100 + decode_ray(sq, rays[sq], kth - base - excl);
+        }
+        base += total;
+    }
+    return -1;
+}
+
+__device__ __forceinline__ int count_of(const int cnt[4]) { return warp_sum(cnt[0] + cnt[1] + cnt[2] + cnt[3]); }
+
+// Virtual N(0,1) logit (Box-Muller) and Gumbel noise of action `act`.
+__device__ __forceinline__ void logit_noise(uint64_t seed, int64_t ge, int64_t ply, int act, float& z, float& g) {
+    const uint4 w = philox((uint32_t)ge, (uint32_t)ply, (uint32_t)act, TAG_LOGIT, seed);
+    const float u1 = u01(w.x), u2 = u01(w.y), u3 = u01(w.z);
+    z = sqrtf(-2.0f * logf(u1)) * cosf(6.2831853071795864f * u2);
+    g = -logf(-logf(u3));
+}
+
+// Choose an action for the current state (rays/cnt already enumerated).
+// Uniform: k = (u32 * n) >> 32 over ascending legal actions.  Gumbel: argmax
+// of logit + Gumbel over legal actions, ties to the smaller action index.
+__device__ void choose(const KArgs& a, const uint16_t* rays, const int cnt[4], int n, int64_t e, int64_t ply,
+                       int lane, int& act, float& lp) {
+    const int64_t ge = a.env_base + e;
+    if (n == 0) {
+        act = -1;
+        lp = 0.0f;
+        return;
+    }
+    if (a.policy == SB_POLICY_UNIFORM) {
+        const uint4 w = philox((uint32_t)ge, (uint32_t)ply, (uint32_t)((uint64_t)ply >> 32), TAG_ACTION, a.seed);
+        act = kth_action((int)mulshift(w.x, (uint32_t)n), cnt, rays, lane);
+        lp = -logf((float)n);
+        return;
+    }
+    float best = -INFINITY, bestz = 0.0f, m = -INFINITY, s = 0.0f;
+    int besta = 0x7fffffff;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int sq = lane + 32 * k;
+        if (sq >= NSQ || cnt[k] == 0) continue;
+        const uint32_t r = rays[sq];
+        for (int j = 0; j < cnt[k]; ++j) {
+            const int ac = sq * 100 + decode_ray(sq, r, j);
+            float z, g;
+            logit_noise(a.seed, ge, ply, ac, z, g);
+            if (a.logits) z = a.logits[e * NACT + ac];
+            const float key = z + g;
+            if (key > best || (key == best && ac < besta)) {
+                best = key;
+                besta = ac;
+                bestz = z;
+            }
+            if (z > m) {
+                s = s * expf(m - z) + 1.0f;
+                m = z;
+            } else {
+                s += expf(z - m);
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ob = __shfl_xor_sync(FULL, best, o), oz = __shfl_xor_sync(FULL, bestz, o);
+        const int oa = __shfl_xor_sync(FULL, besta, o);
+        if (ob > best || (ob == best && oa < besta)) {
+            best = ob;
+            besta = oa;
+            bestz = oz;
+        }
+        const float om = __shfl_xor_sync(FULL, m, o), os = __shfl_xor_sync(FULL, s, o);
+        const float M = fmaxf(m, om);
+        if (M != -INFINITY) {
+            s = (m == -INFINITY ? 0.0f : s * expf(m - M)) + (om == -INFINITY ? 0.0f : os * expf(om - M));
+            m = M;
+        }
+    }
+    act = besta;
+    lp = bestz - (m + logf(s));
+}
+
+// ---------------------------------------------------------------------------
+// Reset (csrc/stratego_buffer.cu:529-618; host part cpp:289-291)
+// ---------------------------------------------------------------------------
+
+__device__ void reset_env(uint8_t* rec, int64_t* ring2, const KArgs& a, int64_t e, bool from_pool, int lane) {
+    const uint8_t* red = nullptr;
+    const uint8_t* blue = nullptr;
+    const int32_t ep = fld<int32_t>(rec, R_EPISODE);
+    if (from_pool) {
+        const int64_t ge = a.env_base + e;
+        const uint4 w = philox((uint32_t)ge, (uint32_t)ep, (uint32_t)((uint64_t)ge >> 32), TAG_RESET, a.seed);
+        const uint64_t ri = ((uint64_t)w.x * (uint64_t)a.pool_size) >> 32;
+        const uint64_t bi = ((uint64_t)w.y * (uint64_t)a.pool_size) >> 32;
+        red = a.pool + ri * 40;
+        blue = a.pool + bi * 40;
+    }
+    uint64_t h = 0;
+    bool bad = false;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int sq = lane + 32 * k;
+        if (sq >= NSQ) continue;
+        int rp, bp;
+        if (from_pool) {
+            rp = sq < 40 ? red[sq] : 0;
+            bp = sq >= 60 ? blue[sq - 60] : 0;
+        } else {
+            rp = a.setup_red[e * NSQ + sq];
+            bp = a.setup_blue[e * NSQ + sq];
+        }
+        uint8_t code = 0;
+        if (rp != 0) {
+            if (rp < 0 || rp > 12) bad = true;
+            else {
+                code = (uint8_t)(rp | C_OCC);
+                h ^= zob(a.zob, sq, 0, rp);
+            }
+        } else if (bp != 0) {
+            if (bp < 0 || bp > 12) bad = true;
+            else {
+                code = (uint8_t)(bp | C_OCC | C_BLUE);
+                h ^= zob(a.zob, sq, 1, bp);
+            }
+        }
+        rec[sq] = code;
+    }
+    h = warp_xor64(h);
+    if (__any_sync(FULL, bad) && lane == 0 && a.status) atomicOr(a.status, SB_STATUS_BAD_SETUP);
+    int4* rg = reinterpret_cast<int4*>(ring2);  // 2 x 64 x 8 B = 64 x 16 B
+    rg[lane] = make_int4(0, 0, 0, 0);
+    rg[lane + 32] = make_int4(0, 0, 0, 0);
+    if (lane < 4) reinterpret_cast<int4*>(rec + R_HIST)[lane] = make_int4(0, 0, 0, 0);
+    if (lane == 0) {
+        fld<int8_t>(rec, R_PLAYER) = 0;
+        fld<int8_t>(rec, R_OUTCOME) = -1;
+        rec[R_TERM] = 0;
+        rec[R_FLAGCAP] = 0;
+        fld<int32_t>(rec, R_MOVENUM) = 0;
+        fld<int32_t>(rec, R_MSA) = 0;
+        fld<int32_t>(rec, R_TSINCE) = 0;
+        rec[R_HHEAD] = 0;
+        rec[R_HLEN] = 0;
+        rec[R_TSVIOL] = 0;
+        rec[R_CHVIOL] = 0;
+        fld<int32_t>(rec, R_TSCOUNT) = 0;
+        fld<int32_t>(rec, R_TSCOUNT + 4) = 0;
+        fld<int16_t>(rec, R_TSLO) = -1;
+        fld<int16_t>(rec, R_TSLO + 2) = -1;
+        fld<int16_t>(rec, R_TSHI) = -1;
+        fld<int16_t>(rec, R_TSHI + 2) = -1;
+        rec[R_CHHEAD] = 0;
+        rec[R_CHHEAD + 1] = 0;
+        rec[R_CHLEN] = 0;
+        rec[R_CHLEN + 1] = 0;
+        fld<int8_t>(rec, R_CHLAST) = -1;
+        fld<int8_t>(rec, R_CHLAST + 1) = -1;
+        fld<int16_t>(rec, R_PROP) = -1;
+        fld<uint64_t>(rec, R_ZHASH) = h;
+        fld<int32_t>(rec, R_EPISODE) = ep + (from_pool ? 1 : 0);
+        fld<int32_t>(rec, R_PROPPLY) = -1;
+        fld<int16_t>(rec, R_NLEGAL) = 0;
+        fld<float>(rec, R_PROPLP) = 0.0f;
+    }
+    __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
+// Apply one action (csrc/stratego_buffer.cu:111-399)
+// ---------------------------------------------------------------------------
+
+// Returns false (and changes nothing) when the action is rejected.  On
+// success the board, counters, history, trackers and the caps part of the
+// terminal check are done; check_legal asks the caller for the "side to move
+// has no legal move" test on the new board.
+__device__ bool apply_env(uint8_t* rec, int64_t* ring2, const KArgs& a, int64_t act, int lane, bool& check_legal,
+                          bool& flag_taken) {
+    check_legal = false;
+    flag_taken = false;
+    if (act < 0 || act >= NACT) return false;
+    const int p = fld<int8_t>(rec, R_PLAYER);
+    const int src = (int)act / 100, dst = (int)act % 100;
+    if (src == dst) return false;
+    const uint8_t cs = rec[src], cd = rec[dst];
+    const int ps = cs & C_PIECE, pd = cd & C_PIECE;
+    if (!(cs & C_OCC) || ((cs >> 4) & 1) != p || !can_move(ps)) return false;
+    if ((cd & C_OCC) && ((cd >> 4) & 1) == p) return false;
+    if (is_lake(dst)) return false;
+    const int sr = src / 10, sc = src % 10, dr = dst / 10, dc = dst % 10;
+    if (sr != dr && sc != dc) return false;
+    if (ps != 2) {
+        const int dist = sr != dr ? abs(dr - sr) : abs(dc - sc);
+        if (dist != 1) return false;
+    } else {
+        const int step = sr != dr ? (dr > sr ? 10 : -10) : (dc > sc ? 1 : -1);
+        for (int q = src + step; q != dst; q += step)
+            if (is_lake(q) || (rec[q] & C_OCC)) return false;
+    }
+    const int opp = 1 - p;
+    const bool attack = (cd & C_OCC) != 0;
+    // 0 plain move, 1 attacker wins, 2 defender wins, 3 both removed
+    int result;
+    int8_t outcome = fld<int8_t>(rec, R_OUTCOME);
+    if (!attack) result = 0;
+    else if (pd == 11) {
+        result = 1;
+        flag_taken = true;
+        outcome = (int8_t)(p == 0 ? 0 : 1);
+    } else if (pd == 12) result = ps == 3 ? 1 : 2;
+    else if (ps == 1 && pd == 10) result = 1;
+    else result = ps > pd ? 1 : (ps < pd ? 2 : 3);
+
+    // moved / revealed flags (cu:243-253)
+    uint8_t fs, fd;
+    if (attack) {
+        fs = (uint8_t)((cs & C_MOVED) | C_REV);
+        fd = (uint8_t)((cd & C_MOVED) | C_REV);
+    } else {
+        fs = C_MOVED;
+        fd = (uint8_t)(C_MOVED | (cs & C_REV));
+    }
+    uint8_t dpart = 0;
+    if (result <= 1) dpart = (uint8_t)(ps | C_OCC | (p ? C_BLUE : 0));
+    else if (result == 2) dpart = (uint8_t)(cd & (C_PIECE | C_BLUE | C_OCC));
+    const uint8_t ns = fs, nd = (uint8_t)(fd | dpart);
+
+    uint64_t h = fld<uint64_t>(rec, R_ZHASH) ^ zob(a.zob, src, p, ps);
+    if (result == 0) h ^= zob(a.zob, dst, p, ps);
+    else if (result == 1) h ^= zob(a.zob, dst, opp, pd) ^ zob(a.zob, dst, p, ps);
+    else if (result == 3) h ^= zob(a.zob, dst, opp, pd);
+
+    const int32_t msa = attack ? 0 : fld<int32_t>(rec, R_MSA) + 1;
+    const int32_t mn = fld<int32_t>(rec, R_MOVENUM) + 1;
+    const int head = rec[R_HHEAD], hlen = rec[R_HLEN];
+
+    // two-square, per mover (cu:272-296)
+    int32_t tsc = fld<int32_t>(rec, R_TSCOUNT + 4 * p);
+    int tslo = fld<int16_t>(rec, R_TSLO + 2 * p), tshi = fld<int16_t>(rec, R_TSHI + 2 * p);
+    uint8_t tsv = rec[R_TSVIOL];
+    if (attack) {
+        tsc = 0;
+        tslo = -1;
+        tshi = -1;
+    } else {
+        const int lo = min(src, dst), hi = max(src, dst);
+        if (tslo == lo && tshi == hi) ++tsc;
+        else {
+            tsc = 1;
+            tslo = lo;
+            tshi = hi;
+        }
+        if (tsc > a.ts_limit) tsv = 1;
+    }
+
+    // chasing (cu:306-381): threat = an opponent piece 4-adjacent to dst on
+    // the new board
+    bool threat = false;
+#pragma unroll
+    for (int d = 0; d < 4; ++d) {
+        int q;
+        if (d == 0) { if (dr == 0) continue; q = dst - 10; }
+        else if (d == 1) { if (dr == 9) continue; q = dst + 10; }
+        else if (d == 2) { if (dc == 0) continue; q = dst - 1; }
+        else { if (dc == 9) continue; q = dst + 1; }
+        if (is_lake(q)) continue;
+        const uint8_t c = q == src ? ns : rec[q];
+        if ((c & C_OCC) && ((c >> 4) & 1) == opp) threat = true;
+    }
+    int chh = rec[R_CHHEAD + p], chl = rec[R_CHLEN + p], chlast = fld<int8_t>(rec, R_CHLAST + p);
+    uint8_t chv = rec[R_CHVIOL];
+    int64_t* ring = ring2 + p * NRING;
+    if (threat) {
+        bool f = false;
+        if (lane < chl) f = (uint64_t)ring[lane] == h;
+        if (lane + 32 < chl) f = f || (uint64_t)ring[lane + 32] == h;
+        const bool found = __any_sync(FULL, f);
+        const bool exc = chlast >= 0 && dst == chlast;
+        if (found && !exc) chv = 1;
+        if (lane == 0) ring[chl < NRING ? chl : chh] = (int64_t)h;
+        if (chl < NRING) ++chl;
+        else chh = (chh + 1) % NRING;
+        chlast = src;
+    } else {
+        chl = 0;
+        chh = 0;
+        chlast = -1;
+    }
+
+    // terminal caps (cu:383-395); the legal-move test is the caller's
+    if (outcome == -1) {
+        if (mn >= a.max_len) outcome = 2;
+        else if (msa >= a.no_attack_limit) outcome = 2;
+        else check_legal = true;
+    }
+
+    if (lane == 0) {
+        rec[src] = ns;
+        rec[dst] = nd;
+        fld<uint64_t>(rec, R_ZHASH) = h;
+        fld<int32_t>(rec, R_MSA) = msa;
+        fld<int32_t>(rec, R_MOVENUM) = mn;
+        fld<int16_t>(rec, R_HIST + 2 * head) = (int16_t)act;
+        rec[R_HHEAD] = (uint8_t)((head + 1) & 31);
+        rec[R_HLEN] = (uint8_t)min(hlen + 1, NHIST);
+        fld<int8_t>(rec, R_PLAYER) = (int8_t)opp;
+        fld<int32_t>(rec, R_TSCOUNT + 4 * p) = tsc;
+        fld<int16_t>(rec, R_TSLO + 2 * p) = (int16_t)tslo;
+        fld<int16_t>(rec, R_TSHI + 2 * p) = (int16_t)tshi;
+        rec[R_TSVIOL] = tsv;
+        rec[R_CHHEAD + p] = (uint8_t)chh;
+        rec[R_CHLEN + p] = (uint8_t)chl;
+        fld<int8_t>(rec, R_CHLAST + p) = (int8_t)chlast;
+        rec[R_CHVIOL] = chv;
+        fld<int8_t>(rec, R_OUTCOME) = outcome;
+        rec[R_TERM] = outcome != -1;
+        if (flag_taken) rec[R_FLAGCAP] = 1;
+        fld<int32_t>(rec, R_PROPPLY) = -1;
+    }
+    __syncwarp();
+    return true;
+}
+
+// ---------------------------------------------------------------------------
+// Observation staging
+// ---------------------------------------------------------------------------
+
+template <typename T>
+struct IV;
+template <>
+struct IV<float> {
+    static __device__ __forceinline__ float from(float f) { return f; }
+};
+template <>
+struct IV<uint16_t> {
+    static __device__ __forceinline__ uint16_t from(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
+};
+
+template <typename T>
+union Chunk {
+    uint4 v;
+    T e[16 / sizeof(T)];
+};
+
+// Infostate of the side to move (stratego/env/infostate.py:37-109, channel
+// meaning as csrc/stratego_buffer.cu:707-767) into the region-1 staging
+// buffer (channels 0-42, padded to 16 bytes) and the history staging buffer
+// (channels 456-487).
+template <typename T>
+__device__ void stage_infostate(const uint8_t* rec, const KArgs& a, int lane, T* r1, T* hs, T* pat_opp, T* pat_own) {
+    constexpr int PB = NSQ * (int)sizeof(T);
+    constexpr int R1B = ((43 * PB + 15) / 16) * 16;
+    constexpr int HB = 32 * PB;
+    const int p = rec[R_PLAYER];
+    const T ONE = IV<T>::from(1.0f), NEG = IV<T>::from(-1.0f), TW = IV<T>::from(__fdiv_rn(1.0f, 12.0f));
+    const T ZERO = IV<T>::from(0.0f);
+    // hidden-piece rows for channels 12-23 (opponent) and 24-35 (own);
+    // one period = 400 bytes (two bf16 planes or one f32 plane)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int sq = lane + 32 * k;
+        if (sq >= NSQ) continue;
+        const uint8_t c = rec[sq];
+        const bool occ = c & C_OCC, rev = c & C_REV;
+        const bool own = occ && ((c >> 4) & 1) == p, opp = occ && !own;
+        const T vo = (opp && !rev) ? TW : ZERO, vw = (own && !rev) ? TW : ZERO;
+        pat_opp[sq] = vo;
+        pat_own[sq] = vw;
+        if (sizeof(T) == 2) {
+            pat_opp[NSQ + sq] = vo;
+            pat_own[NSQ + sq] = vw;
+        }
+    }
+    __syncwarp();
+    const int mn = fld<int32_t>(rec, R_MOVENUM), msa = fld<int32_t>(rec, R_MSA);
+    const T v41 = IV<T>::from(a.max_len > 0 ? __fdiv_rn((float)mn, (float)a.max_len) : 0.0f);
+    const T v42 = IV<T>::from(a.no_attack_limit > 0 ? __fdiv_rn((float)msa, (float)a.no_attack_limit) : 0.0f);
+    uint8_t* r1b = reinterpret_cast<uint8_t*>(r1);
+    for (int i = lane; i < R1B / 16; i += 32) {
+        const int off = i * 16;
+        Chunk<T> ch;
+        if (off >= 12 * PB && off < 36 * PB) {
+            const bool o = off < 24 * PB;
+            const uint8_t* row = reinterpret_cast<const uint8_t*>(o ? pat_opp : pat_own);
+            ch.v = *reinterpret_cast<const uint4*>(row + (off - (o ? 12 : 24) * PB) % 400);
+        } else if (off + 16 > 41 * PB && off < 43 * PB) {
+#pragma unroll
+            for (int j = 0; j < 16 / (int)sizeof(T); ++j) {
+                const int pl = (off + j * (int)sizeof(T)) / PB;
+                ch.e[j] = pl == 41 ? v41 : (pl == 42 ? v42 : ZERO);
+            }
+        } else {
+            ch.v = make_uint4(0, 0, 0, 0);
+        }
+        *reinterpret_cast<uint4*>(r1b + off) = ch.v;
+    }
+    uint8_t* hsb = reinterpret_cast<uint8_t*>(hs);
+    for (int i = lane; i < HB / 16; i += 32) *reinterpret_cast<uint4*>(hsb + i * 16) = make_uint4(0, 0, 0, 0);
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int sq = lane + 32 * k;
+        if (sq >= NSQ) continue;
+        const uint8_t c = rec[sq];
+        const int pc = c & C_PIECE;
+        const bool rev = c & C_REV, mov = c & C_MOVED;
+        if (!(c & C_OCC)) {
+            r1[38 * NSQ + sq] = ONE;
+        } else if (((c >> 4) & 1) == p) {
+            r1[(pc - 1) * NSQ + sq] = ONE;
+            r1[(rev ? 24 + pc - 1 : 36) * NSQ + sq] = ONE;
+            if (mov) r1[39 * NSQ + sq] = ONE;
+        } else {
+            r1[(rev ? 12 + pc - 1 : 37) * NSQ + sq] = ONE;
+            if (mov) r1[40 * NSQ + sq] = ONE;
+        }
+    }
+    const int hl = rec[R_HLEN], hh = rec[R_HHEAD];
+    if (lane < hl) {
+        const int slot = (hh - 1 - lane) & 31;
+        const int act = fld<int16_t>(rec, R_HIST + 2 * slot);
+        hs[lane * NSQ + act % 100] = ONE;
+        hs[lane * NSQ + act / 100] = NEG;
+    }
+}
+
+// u8 legal mask of the side to move (csrc/stratego_buffer.cu:448-507) from
+// the packed rays into a zeroed 10,000-byte staging buffer.
+__device__ void stage_mask_u8(const uint16_t* rays, int lane, uint8_t* m) {
+    for (int i = lane; i < NACT / 16; i += 32) reinterpret_cast<uint4*>(m)[i] = make_uint4(0, 0, 0, 0);
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int sq = lane + 32 * k;
+        if (sq >= NSQ) continue;
+        const uint32_t r = rays[sq];
+        if (!r) continue;
+        uint8_t* row = m + sq * 100;
+        const int up = r & 15, left = (r >> 4) & 15, right = (r >> 8) & 15, down = r >> 12;
+        for (int j = 1; j <= up; ++j) row[sq - 10 * j] = 1;
+        for (int j = 1; j <= left; ++j) row[sq - j] = 1;
+        for (int j = 1; j <= right; ++j) row[sq + j] = 1;
+        for (int j = 1; j <= down; ++j) row[sq + 10 * j] = 1;
+    }
+}
+
+// bit-packed mask: bit j of byte k = flat action 8k+j.
+__device__ void stage_mask_bits(const uint16_t* rays, int lane, uint32_t* w) {
+    for (int i = lane; i < 79; i += 32) reinterpret_cast<uint4*>(w)[i] = make_uint4(0, 0, 0, 0);
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int sq = lane + 32 * k;
+        if (sq >= NSQ) continue;
+        const uint32_t r = rays[sq];
+        if (!r) continue;
+        const int up = r & 15, left = (r >> 4) & 15, right = (r >> 8) & 15, down = r >> 12;
+        const int n = up + left + right + down;
+        for (int j = 0; j < n; ++j) {
+            const int f = sq * 100 + decode_ray(sq, r, j);
+            atomicOr(&w[f >> 5], 1u << (f & 31));
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// The per-env kernel
+// ---------------------------------------------------------------------------
+
+template <typename T>
+__global__ void __launch_bounds__(WARPS * 32) env_kernel(const KArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int lane = threadIdx.x & 31;
+    uint8_t* ws = smem + (threadIdx.x >> 5) * a.sm_warp;
+    uint8_t* rec = ws;
+    uint16_t* rays = reinterpret_cast<uint16_t*>(ws + SM_RAYS);
+    bool staged = false;
+    const int64_t nwarps = (int64_t)gridDim.x * WARPS;
+    for (int64_t e = (int64_t)blockIdx.x * WARPS + (threadIdx.x >> 5); e < a.n; e += nwarps) {
+        reinterpret_cast<uint2*>(rec)[lane] = reinterpret_cast<const uint2*>(a.rec + e * REC)[lane];
+        __syncwarp();
+        int64_t* ring2 = a.ring + e * 2 * NRING;
+        bool dirty = false;
+        int cnt[4];
+
+        if ((a.flags & (F_RESET_PLANES | F_RESET_POOL)) && ((a.flags & F_FORCE) || rec[R_TERM])) {
+            reset_env(rec, ring2, a, e, (a.flags & F_RESET_POOL) != 0, lane);
+            dirty = true;
+        }
+
+        if (a.flags & F_APPLY) {
+            const bool was_term = rec[R_TERM] != 0;
+            int64_t act = -1;
+            float lp = 0.0f;
+            if (!was_term) {
+                int n_legal = -1;
+                if (a.actions) act = a.actions[e];
+                if (!a.actions || (a.flags & F_STEP)) {
+                    if (fld<int32_t>(rec, R_PROPPLY) == (int32_t)a.ply && rec[R_PROPKIND] == a.policy &&
+                        !a.logits) {
+                        n_legal = fld<int16_t>(rec, R_NLEGAL);
+                        if (!a.actions) {
+                            act = fld<int16_t>(rec, R_PROP);
+                            lp = fld<float>(rec, R_PROPLP);
+                        }
+                    } else {
+                        enumerate(rec, rec[R_PLAYER], rays, lane, cnt);
+                        n_legal = count_of(cnt);
+                        if (!a.actions) {
+                            int ac;
+                            choose(a, rays, cnt, n_legal, e, a.ply, lane, ac, lp);
+                            act = ac;
+                        }
+                    }
+                }
+                if ((a.flags & F_STEP) && n_legal == 0) {
+                    // a start position whose side to move cannot move: it
+                    // loses (the rule of stratego/env/rules.py:406-413)
+                    if (lane == 0) {
+                        fld<int8_t>(rec, R_OUTCOME) = (int8_t)(rec[R_PLAYER] == 0 ? 1 : 0);
+                        rec[R_TERM] = 1;
+                        fld<int32_t>(rec, R_PROPPLY) = -1;
+                    }
+                    act = -1;
+                    __syncwarp();
+                } else {
+                    bool chk, flag;
+                    const bool ok = apply_env(rec, ring2, a, act, lane, chk, flag);
+                    if (!ok) {
+                        if (lane == 0) fld<int32_t>(rec, R_INVALID) += 1;
+                    } else if (chk) {
+                        enumerate(rec, rec[R_PLAYER], rays, lane, cnt);
+                        if (count_of(cnt) == 0 && lane == 0) {
+                            fld<int8_t>(rec, R_OUTCOME) = (int8_t)(rec[R_PLAYER] == 0 ? 1 : 0);
+                            rec[R_TERM] = 1;
+                        }
+                    }
+                    __syncwarp();
+                }
+            }
+            const bool term = rec[R_TERM] != 0;
+            if (lane == 0) {
+                if (term) fld<int32_t>(rec, R_TSINCE) += 1;
+                const int8_t oc = fld<int8_t>(rec, R_OUTCOME);
+                if (a.reward) a.reward[e] = oc == 0 ? 1.0f : (oc == 1 ? -1.0f : 0.0f);
+                if (a.done) a.done[e] = term ? 1 : 0;
+                if (a.action_taken) a.action_taken[e] = act;
+                if (a.logprob_taken) a.logprob_taken[e] = lp;
+                if (a.stats && term && !was_term) {
+                    atomicAdd(reinterpret_cast<unsigned long long*>(&a.stats[0]), 1ull);
+                    atomicAdd(reinterpret_cast<unsigned long long*>(&a.stats[oc == 0 ? 1 : (oc == 1 ? 2 : 3)]), 1ull);
+                    atomicAdd(reinterpret_cast<unsigned long long*>(&a.stats[4]),
+                              (unsigned long long)fld<int32_t>(rec, R_MOVENUM));
+                }
+            }
+            __syncwarp();
+            dirty = true;
+            if ((a.flags & F_AUTO_RESET) && term) reset_env(rec, ring2, a, e, true, lane);
+        }
+
+        const bool observe = (a.flags & (F_MASK_U8 | F_MASK_BITS | F_PROPOSE | F_HAS_LEGAL | F_SAMPLE_OUT)) != 0;
+        if (observe) {
+            enumerate(rec, rec[R_PLAYER], rays, lane, cnt);
+            const int n = count_of(cnt);
+            __syncwarp();
+            if (a.flags & (F_PROPOSE | F_SAMPLE_OUT)) {
+                const int64_t pp = (a.flags & F_PROPOSE) ? a.propose_ply : a.ply;
+                int ac;
+                float lp;
+                choose(a, rays, cnt, n, e, pp, lane, ac, lp);
+                if (lane == 0) {
+                    if (a.flags & F_PROPOSE) {
+                        fld<int16_t>(rec, R_PROP) = (int16_t)ac;
+                        fld<int32_t>(rec, R_PROPPLY) = a.logits ? -1 : (int32_t)pp;
+                        rec[R_PROPKIND] = (uint8_t)a.policy;
+                        fld<int16_t>(rec, R_NLEGAL) = (int16_t)n;
+                        fld<float>(rec, R_PROPLP) = lp;
+                        if (a.next_action) a.next_action[e] = (int16_t)ac;
+                        if (a.next_logprob) a.next_logprob[e] = lp;
+                    }
+                    if (a.flags & F_SAMPLE_OUT) {
+                        if (a.sampled) a.sampled[e] = ac;
+                        if (a.sampled_lp) a.sampled_lp[e] = lp;
+                    }
+                }
+                if (a.flags & F_PROPOSE) dirty = true;
+            }
+            if ((a.flags & F_HAS_LEGAL) && lane == 0) a.has_legal[e] = n > 0;
+        }
+        if ((a.flags & F_HASH) && lane == 0) a.hash[e] = fld<int64_t>(rec, R_ZHASH);
+
+        if (a.flags & (F_MASK_U8 | F_MASK_BITS | F_INFO)) {
+            if (staged && lane == 0) bulk_wait_read();
+            __syncwarp();
+            bool issue = false;
+            if (a.flags & F_MASK_U8) {
+                stage_mask_u8(rays, lane, ws + a.sm_mask);
+                issue = true;
+            }
+            if (a.flags & F_MASK_BITS) stage_mask_bits(rays, lane, reinterpret_cast<uint32_t*>(ws + a.sm_bits));
+            if (a.flags & F_INFO) {
+                stage_infostate<T>(rec, a, lane, reinterpret_cast<T*>(ws + a.sm_r1), reinterpret_cast<T*>(ws + a.sm_hist),
+                                   reinterpret_cast<T*>(ws + SM_PAT_OPP), reinterpret_cast<T*>(ws + SM_PAT_OWN));
+                issue = true;
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (a.flags & F_MASK_BITS) {
+                const uint16_t* src = reinterpret_cast<const uint16_t*>(ws + a.sm_bits);
+                uint16_t* dst = reinterpret_cast<uint16_t*>(a.mask_bits + e * SB_MASK_BITS_BYTES);
+                for (int i = lane; i < SB_MASK_BITS_BYTES / 2; i += 32) dst[i] = src[i];
+            }
+            if (a.flags & F_INFO) {
+                constexpr int PB = NSQ * (int)sizeof(T);
+                constexpr int R1B = ((43 * PB + 15) / 16) * 16;
+                const bool compact = a.info_layout == SB_LAYOUT_COMPACT;
+                uint8_t* base = reinterpret_cast<uint8_t*>(a.info) + e * (int64_t)(compact ? 76 : NCH) * PB;
+                if (a.info_layout == SB_LAYOUT_DENSE_ALL) {
+                    for (int i = R1B / 16 + lane; i < 456 * PB / 16; i += 32)
+                        reinterpret_cast<uint4*>(base)[i] = make_uint4(0, 0, 0, 0);
+                }
+                if (lane == 0) {
+                    bulk_s2g(base, ws + a.sm_r1, R1B);
+                    bulk_s2g(base + (compact ? 44 : 456) * PB, ws + a.sm_hist, 32 * PB);
+                }
+            }
+            if ((a.flags & F_MASK_U8) && lane == 0) bulk_s2g(a.mask_u8 + e * NACT, ws + a.sm_mask, NACT);
+            if (issue) {
+                if (lane == 0) bulk_commit();
+                staged = true;
+            }
+        }
+
+        if (dirty) {
+            __syncwarp();
+            reinterpret_cast<uint2*>(a.rec + e * REC)[lane] = reinterpret_cast<const uint2*>(rec)[lane];
+        }
+        __syncwarp();
+    }
+    if (staged && lane == 0) bulk_wait_all();
+}
+
+// ---------------------------------------------------------------------------
+// Small kernels
+// ---------------------------------------------------------------------------
+
+__global__ void hello_kernel(int32_t* out) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) out[0] = 42;
+}
+
+// Fresh-buffer state (csrc/stratego_buffer.cpp:24-55).
+__global__ void init_kernel(uint8_t* rec, int64_t* ring, int64_t n) {
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= n) return;
+    uint8_t* r = rec + e * REC;
+    for (int i = 0; i < REC / 16; ++i) reinterpret_cast<int4*>(r)[i] = make_int4(0, 0, 0, 0);
+    fld<int8_t>(r, R_OUTCOME) = -1;
+    fld<int16_t>(r, R_TSLO) = -1;
+    fld<int16_t>(r, R_TSLO + 2) = -1;
+    fld<int16_t>(r, R_TSHI) = -1;
+    fld<int16_t>(r, R_TSHI + 2) = -1;
+    fld<int8_t>(r, R_CHLAST) = -1;
+    fld<int8_t>(r, R_CHLAST + 1) = -1;
+    fld<int16_t>(r, R_PROP) = -1;
+    fld<int32_t>(r, R_PROPPLY) = -1;
+    int4* g = reinterpret_cast<int4*>(ring + e * 2 * NRING);
+    for (int i = 0; i < 2 * NRING / 2; ++i) g[i] = make_int4(0, 0, 0, 0);
+}
+
+// Pool entry i: Fisher-Yates over the roster, Philox words (ctr: i_lo, block,
+// i_hi, TAG_SETUP), j = (w * (i+1)) >> 32.
+__global__ void pool_kernel(uint64_t seed, int64_t start, int64_t count, uint8_t* out) {
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= count) return;
+    const uint64_t idx = (uint64_t)(start + t);
+    uint8_t p[40];
+    const uint8_t counts[13] = {0, 1, 8, 5, 4, 4, 4, 3, 2, 1, 1, 1, 6};
+    int k = 0;
+    for (int pt = 1; pt <= 12; ++pt)
+        for (int j = 0; j < counts[pt]; ++j) p[k++] = (uint8_t)pt;
+    for (int blk = 0; blk < 10; ++blk) {
+        const uint4 w = philox((uint32_t)idx, (uint32_t)blk, (uint32_t)(idx >> 32), TAG_SETUP, seed);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        for (int q = 0; q < 4; ++q) {
+            const int d = blk * 4 + q;
+            if (d >= 39) break;
+            const int i = 39 - d;
+            const int j = (int)mulshift(ws[q], (uint32_t)(i + 1));
+            const uint8_t tmp = p[i];
+            p[i] = p[j];
+            p[j] = tmp;
+        }
+    }
+    for (int i = 0; i < 40; ++i) out[t * 40 + i] = p[i];
+}
+
+__global__ void export_kernel(const uint8_t* rec, int64_t n, sb_export o) {
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= n) return;
+    const uint8_t* r = rec + e * REC;
+    for (int q = 0; q < NSQ; ++q) {
+        const uint8_t c = r[q];
+        if (o.board_owner) o.board_owner[e * NSQ + q] = (int8_t)owner_of(c);
+        if (o.board_piece) o.board_piece[e * NSQ + q] = (int8_t)((c & C_OCC) ? (c & C_PIECE) : 0);
+        if (o.moved_squares) o.moved_squares[e * NSQ + q] = (c & C_MOVED) ? 1 : 0;
+        if (o.revealed_squares) o.revealed_squares[e * NSQ + q] = (c & C_REV) ? 1 : 0;
+    }
+    const int8_t oc = *reinterpret_cast<const int8_t*>(r + R_OUTCOME);
+    if (o.current_player) o.current_player[e] = *reinterpret_cast<const int8_t*>(r + R_PLAYER);
+    if (o.outcome) o.outcome[e] = oc;
+    if (o.terminated) o.terminated[e] = r[R_TERM];
+    if (o.flag_captured) o.flag_captured[e] = r[R_FLAGCAP];
+    if (o.move_number) o.move_number[e] = *reinterpret_cast<const int32_t*>(r + R_MOVENUM);
+    if (o.moves_since_attack) o.moves_since_attack[e] = *reinterpret_cast<const int32_t*>(r + R_MSA);
+    if (o.terminated_since) o.terminated_since[e] = *reinterpret_cast<const int32_t*>(r + R_TSINCE);
+    if (o.move_history)
+        for (int i = 0; i < NHIST; ++i) o.move_history[e * NHIST + i] = *reinterpret_cast<const int16_t*>(r + R_HIST + 2 * i);
+    if (o.move_history_head) o.move_history_head[e] = r[R_HHEAD];
+    if (o.move_history_len) o.move_history_len[e] = r[R_HLEN];
+    for (int p = 0; p < 2; ++p) {
+        if (o.two_square_count) o.two_square_count[e * 2 + p] = *reinterpret_cast<const int32_t*>(r + R_TSCOUNT + 4 * p);
+        if (o.two_square_pair_lo) o.two_square_pair_lo[e * 2 + p] = *reinterpret_cast<const int16_t*>(r + R_TSLO + 2 * p);
+        if (o.two_square_pair_hi) o.two_square_pair_hi[e * 2 + p] = *reinterpret_cast<const int16_t*>(r + R_TSHI + 2 * p);
+        if (o.chase_hash_head) o.chase_hash_head[e * 2 + p] = r[R_CHHEAD + p];
+        if (o.chase_hash_len) o.chase_hash_len[e * 2 + p] = r[R_CHLEN + p];
+        if (o.chase_last_src) o.chase_last_src[e * 2 + p] = *reinterpret_cast<const int8_t*>(r + R_CHLAST + p);
+    }
+    if (o.two_square_violation) o.two_square_violation[e] = r[R_TSVIOL];
+    if (o.chasing_violation) o.chasing_violation[e] = r[R_CHVIOL];
+    if (o.episode) o.episode[e] = *reinterpret_cast<const int32_t*>(r + R_EPISODE);
+    if (o.invalid_count) o.invalid_count[e] = *reinterpret_cast<const int32_t*>(r + R_INVALID);
+    if (o.reward) o.reward[e] = oc == 0 ? 1.0f : (oc == 1 ? -1.0f : 0.0f);
+}
+
+__global__ void sum_move_kernel(const uint8_t* rec, int64_t n, int64_t* out) {
+    int64_t acc = 0;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x)
+        acc += *reinterpret_cast<const int32_t*>(rec + e * REC + R_MOVENUM);
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(FULL, acc, o);
+    if ((threadIdx.x & 31) == 0 && acc) atomicAdd(reinterpret_cast<unsigned long long*>(out), (unsigned long long)acc);
+}
+
+}  // namespace sb
+
+// ===========================================================================
+// Host side: argument checks, launch configuration, C ABI
+// ===========================================================================
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(SB_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int check_state(const sb_state* s) {
+    if (!s) return fail(SB_E_ARG, "state is NULL");
+    if (s->n < 0) return fail(SB_E_ARG, "n < 0");
+    if (s->n == 0) return SB_OK;
+    if (!s->records || !s->chase_ring || !s->zobrist) return fail(SB_E_ARG, "records/chase_ring/zobrist is NULL");
+    if (!aligned(s->records, 16) || !aligned(s->chase_ring, 16)) return fail(SB_E_ARG, "records/chase_ring not 16-byte aligned");
+    if (s->setup_pool && s->pool_size <= 0) return fail(SB_E_ARG, "setup_pool given with pool_size <= 0");
+    if (s->pool_size > 0xFFFFFFFFll) return fail(SB_E_ARG, "pool_size above 2^32");
+    return SB_OK;
+}
+
+sb::KArgs base_args(const sb_state* s) {
+    sb::KArgs k;
+    memset(&k, 0, sizeof k);
+    k.rec = s->records;
+    k.ring = s->chase_ring;
+    k.zob = s->zobrist;
+    k.pool = s->setup_pool;
+    k.pool_size = s->pool_size;
+    k.n = s->n;
+    k.env_base = s->env_base;
+    k.seed = s->seed;
+    k.no_attack_limit = s->no_attack_limit;
+    k.max_len = s->max_game_length;
+    k.ts_limit = s->two_square_limit;
+    k.status = s->status;
+    k.policy = SB_POLICY_UNIFORM;
+    return k;
+}
+
+struct OccEntry {
+    const void* fn;
+    int dev;
+    int smem;
+    int blocks;
+};
+std::mutex g_mu;
+OccEntry g_occ[64];
+int g_nocc = 0;
+
+int blocks_per_sm(const void* fn, int dev, int smem, int* out) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    for (int i = 0; i < g_nocc; ++i)
+        if (g_occ[i].fn == fn && g_occ[i].dev == dev && g_occ[i].smem == smem) {
+            *out = g_occ[i].blocks;
+            return SB_OK;
+        }
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    int nb = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, sb::WARPS * 32, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    if (nb < 1) return fail(SB_E_CUDA, "kernel does not fit on an SM with %d bytes of shared memory", smem);
+    if (g_nocc < 64) g_occ[g_nocc++] = OccEntry{fn, dev, smem, nb};
+    *out = nb;
+    return SB_OK;
+}
+
+int sm_count(int dev, int* out) {
+    static int cache[64] = {0};
+    if (dev < 0 || dev >= 64) return fail(SB_E_ARG, "device index out of range");
+    if (!cache[dev]) {
+        int v = 0;
+        cudaError_t e = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+        cache[dev] = v;
+    }
+    *out = cache[dev];
+    return SB_OK;
+}
+
+// Shared memory plan of one warp: record, rays, two hidden-piece rows, then
+// the staging buffers that this launch needs.
+void plan_smem(sb::KArgs& k, bool info, int dtype) {
+    int off = sb::SM_FIXED;
+    k.sm_r1 = k.sm_hist = k.sm_mask = k.sm_bits = 0;
+    if (info) {
+        const int pb = dtype == SB_DTYPE_F32 ? 400 : 200;
+        k.sm_r1 = off;
+        off += ((43 * pb + 15) / 16) * 16;
+        k.sm_hist = off;
+        off += 32 * pb;
+    }
+    if (k.flags & sb::F_MASK_U8) {
+        k.sm_mask = off;
+        off += sb::NACT;
+    }
+    if (k.flags & sb::F_MASK_BITS) {
+        k.sm_bits = off;
+        off += 1264;
+    }
+    k.sm_warp = (off + 127) / 128 * 128;
+}
+
+int launch_env(sb::KArgs& k, int dtype, cudaStream_t st) {
+    if (k.n == 0) return SB_OK;
+    plan_smem(k, (k.flags & sb::F_INFO) != 0, dtype);
+    const void* fn = dtype == SB_DTYPE_F32 ? (const void*)sb::env_kernel<float> : (const void*)sb::env_kernel<uint16_t>;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    const int smem = sb::WARPS * k.sm_warp;
+    int nb = 0, sms = 0, rc;
+    if ((rc = blocks_per_sm(fn, dev, smem, &nb)) != SB_OK) return rc;
+    if ((rc = sm_count(dev, &sms)) != SB_OK) return rc;
+    int64_t blocks = (k.n + sb::WARPS - 1) / sb::WARPS;
+    const int64_t cap = (int64_t)sms * nb;
+    if (blocks > cap) blocks = cap;
+    if (dtype == SB_DTYPE_F32)
+        sb::env_kernel<float><<<(unsigned)blocks, sb::WARPS * 32, smem, st>>>(k);
+    else
+        sb::env_kernel<uint16_t><<<(unsigned)blocks, sb::WARPS * 32, smem, st>>>(k);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "env_kernel launch");
+    return SB_OK;
+}
+
+int check_info(const void* p, int dtype, int layout) {
+    if (dtype != SB_DTYPE_F32 && dtype != SB_DTYPE_BF16) return fail(SB_E_ARG, "bad infostate dtype %d", dtype);
+    if (layout < SB_LAYOUT_DENSE_ALL || layout > SB_LAYOUT_COMPACT) return fail(SB_E_ARG, "bad infostate layout %d", layout);
+    if (!aligned(p, 16)) return fail(SB_E_ARG, "infostate buffer not 16-byte aligned");
+    return SB_OK;
+}
+
+int check_policy(const sb_policy* pol) {
+    if (!pol) return SB_OK;
+    if (pol->kind != SB_POLICY_UNIFORM && pol->kind != SB_POLICY_GUMBEL) return fail(SB_E_ARG, "bad policy %d", pol->kind);
+    if (pol->logits && pol->kind != SB_POLICY_GUMBEL) return fail(SB_E_ARG, "logits need SB_POLICY_GUMBEL");
+    return SB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int sb_abi_version(void) { return SB_ABI_VERSION; }
+
+const char* sb_last_error(void) { return g_err; }
+
+int sb_hello_world(int32_t* out, void* stream) {
+    if (!out) return fail(SB_E_ARG, "out is NULL");
+    sb::hello_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(out);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? SB_OK : cuda_fail(e, "hello_kernel launch");
+}
+
+int sb_init_state(const sb_state* s, void* stream) {
+    int rc = check_state(s);
+    if (rc != SB_OK || s->n == 0) return rc;
+    const int64_t blocks = (s->n + 127) / 128;
+    sb::init_kernel<<<(unsigned)blocks, 128, 0, (cudaStream_t)stream>>>(s->records, s->chase_ring, s->n);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? SB_OK : cuda_fail(e, "init_kernel launch");
+}
+
+int sb_reset_planes(const sb_state* s, const int8_t* setup_red, const int8_t* setup_blue, int force_all,
+                    void* stream) {
+    int rc = check_state(s);
+    if (rc != SB_OK || s->n == 0) return rc;
+    if (!setup_red || !setup_blue) return fail(SB_E_ARG, "setup planes are NULL");
+    sb::KArgs k = base_args(s);
+    k.flags = sb::F_RESET_PLANES | (force_all ? sb::F_FORCE : 0);
+    k.setup_red = setup_red;
+    k.setup_blue = setup_blue;
+    return launch_env(k, SB_DTYPE_F32, (cudaStream_t)stream);
+}
+
+int sb_reset_pool(const sb_state* s, int force_all, void* stream) {
+    int rc = check_state(s);
+    if (rc != SB_OK || s->n == 0) return rc;
+    if (!s->setup_pool) return fail(SB_E_NOPOOL, "no setup pool");
+    sb::KArgs k = base_args(s);
+    k.flags = sb::F_RESET_POOL | (force_all ? sb::F_FORCE : 0);
+    return launch_env(k, SB_DTYPE_F32, (cudaStream_t)stream);
+}
+
+int sb_make_setup_pool(uint64_t seed, int64_t start, int64_t count, uint8_t* out, void* stream) {
+    if (count < 0 || start < 0) return fail(SB_E_ARG, "negative pool range");
+    if (count == 0) return SB_OK;
+    if (!out) return fail(SB_E_ARG, "out is NULL");
+    const int64_t blocks = (count + 127) / 128;
+    sb::pool_kernel<<<(unsigned)blocks, 128, 0, (cudaStream_t)stream>>>(seed, start, count, out);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? SB_OK : cuda_fail(e, "pool_kernel launch");
+}
+
+int sb_apply_actions(const sb_state* s, const int64_t* actions, void* stream) {
+    int rc = check_state(s);
+    if (rc != SB_OK || s->n == 0) return rc;
+    if (!actions) return fail(SB_E_ARG, "actions is NULL");
+    sb::KArgs k = base_args(s);
+    k.flags = sb::F_APPLY;
+    k.actions = actions;
+    return launch_env(k, SB_DTYPE_F32, (cudaStream_t)stream);
+}
+
+int sb_step(const sb_state* s, const int64_t* actions, int64_t ply, const sb_policy* policy, int auto_reset,
+            const sb_step_out* out, void* stream) {
+    int rc = check_state(s);
+    if (rc != SB_OK || s->n == 0) return rc;
+    if ((rc = check_policy(policy)) != SB_OK) return rc;
+    if (auto_reset && !s->setup_pool) return fail(SB_E_NOPOOL, "auto_reset needs a setup pool");
+    sb_step_out o;
+    memset(&o, 0, sizeof o);
+    if (out) o = *out;
+    sb::KArgs k = base_args(s);
+    k.flags = sb::F_APPLY | sb::F_STEP | sb::F_PROPOSE | (auto_reset ? sb::F_AUTO_RESET : 0);
+    k.actions = actions;
+    k.ply = ply;
+    k.propose_ply = ply + 1;
+    if (policy) {
+        k.policy = policy->kind;
+        k.logits = policy->logits;
+    }
+    int dtype = SB_DTYPE_F32;
+    if (o.infostate) {
+        if ((rc = check_info(o.infostate, o.info_dtype, o.info_layout)) != SB_OK) return rc;
+        k.flags |= sb::F_INFO;
+        k.info = o.infostate;
+        k.info_layout = o.info_layout;
+        dtype = o.info_dtype;
+    }
+    if (o.mask_u8) {
+        if (!aligned(o.mask_u8, 16)) return fail(SB_E_ARG, "mask_u8 not 16-byte aligned");
+        k.flags |= sb::F_MASK_U8;
+        k.mask_u8 = o.mask_u8;
+    }
+    if (o.mask_bits) {
+        if (!aligned(o.mask_bits, 2)) return fail(SB_E_ARG, "mask_bits not 2-byte aligned");
+        k.flags |= sb::F_MASK_BITS;
+        k.mask_bits = o.mask_bits;
+    }
+    if (o.hash) k.flags |= sb::F_HASH;
+    k.hash = o.hash;
+    k.reward = o.reward;
+    k.done = o.done;
+    k.action_taken = o.action_taken;
+    k.logprob_taken = o.logprob_taken;
+    k.next_action = o.next_action;
+    k.next_logprob = o.next_logprob;
+    k.stats = o.stats;
+    return launch_env(k, dtype, (cudaStream_t)stream);
+}
+
+int sb_sample_actions(const sb_state* s, int64_t ply, const sb_policy* policy, int64_t* actions, float* logprob,
+                      void* stream) {
+    int rc = check_state(s);
+    if (rc != SB_OK || s->n == 0) return rc;
+    if ((rc = check_policy(policy)) != SB_OK) return rc;
+    sb::KArgs k = base_args(s);
+    k.flags = sb::F_SAMPLE_OUT;
+    k.ply = ply;
+    if (policy) {
+        k.policy = policy->kind;
+        k.logits = policy->logits;
+    }
+    k.sampled = actions;
+    k.sampled_lp = logprob;
+    return launch_env(k, SB_DTYPE_F32, (cudaStream_t)stream);
+}
+
+int sb_legal_mask_u8(const sb_state* s, uint8_t* mask, void* stream) {
+    int rc = check_state(s);
+    if (rc != SB_OK || s->n == 0) return rc;
+    if (!mask || !aligned(mask, 16)) return fail(SB_E_ARG, "mask NULL or not 16-byte aligned");
+    sb::KArgs k = base_args(s);
+    k.flags = sb::F_MASK_U8;
+    k.mask_u8 = mask;
+    return launch_env(k, SB_DTYPE_F32, (cudaStream_t)stream);
+}
+
+int sb_legal_mask_bits(const sb_state* s, uint8_t* bits, void* stream) {
+    int rc = check_state(s);
+    if (rc != SB_OK || s->n == 0) return rc;
+    if (!bits || !aligned(bits, 2)) return fail(SB_E_ARG, "bits NULL or not 2-byte aligned");
+    sb::KArgs k = base_args(s);
+    k.flags = sb::F_MASK_BITS;
+    k.mask_bits = bits;
+    return launch_env(k, SB_DTYPE_F32, (cudaStream_t)stream);
+}
+
+int sb_infostate(const sb_state* s, void* out, int dtype, int layout, void* stream) {
+    int rc = check_state(s);
+    if (rc != SB_OK || s->n == 0) return rc;
+    if (!out) return fail(SB_E_ARG, "out is NULL");
+    if ((rc = check_info(out, dtype, layout)) != SB_OK) return rc;
+    sb::KArgs k = base_args(s);
+    k.flags = sb::F_INFO;
+    k.info = out;
+    k.info_layout = layout;
+    return launch_env(k, dtype, (cudaStream_t)stream);
+}
+
+int sb_hash_board(const sb_state* s, int64_t* out, void* stream) {
+    int rc = check_state(s);
+    if (rc != SB_OK || s->n == 0) return rc;
+    if (!out) return fail(SB_E_ARG, "out is NULL");
+    sb::KArgs k = base_args(s);
+    k.flags = sb::F_HASH;
+    k.hash = out;
+    return launch_env(k, SB_DTYPE_F32, (cudaStream_t)stream);
+}
+
+int sb_has_legal_movement(const sb_state* s, uint8_t* out, void* stream) {
+    int rc = check_state(s);
+    if (rc != SB_OK || s->n == 0) return rc;
+    if (!out) return fail(SB_E_ARG, "out is NULL");
+    sb::KArgs k = base_args(s);
+    k.flags = sb::F_HAS_LEGAL;
+    k.has_legal = out;
+    return launch_env(k, SB_DTYPE_F32, (cudaStream_t)stream);
+}
+
+int sb_export_state(const sb_state* s, const sb_export* out, void* stream) {
+    int rc = check_state(s);
+    if (rc != SB_OK || s->n == 0) return rc;
+    if (!out) return fail(SB_E_ARG, "out is NULL");
+    const int64_t blocks = (s->n + 127) / 128;
+    sb::export_kernel<<<(unsigned)blocks, 128, 0, (cudaStream_t)stream>>>(s->records, s->n, *out);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? SB_OK : cuda_fail(e, "export_kernel launch");
+}
+
+int sb_sum_move_number(const sb_state* s, int64_t* out, void* stream) {
+    int rc = check_state(s);
+    if (rc != SB_OK) return rc;
+    if (!out) return fail(SB_E_ARG, "out is NULL");
+    cudaError_t e = cudaMemsetAsync(out, 0, sizeof(int64_t), (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+    if (s->n == 0) return SB_OK;
+    int64_t blocks = (s->n + 255) / 256;
+    if (blocks > 1024) blocks = 1024;
+    sb::sum_move_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(s->records, s->n, out);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? SB_OK : cuda_fail(e, "sum_move_kernel launch");
+}
+
+}  // extern "C"

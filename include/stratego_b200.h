@@ -1,0 +1,206 @@
+/*
+ * stratego_b200.h -- C ABI of the B200 StrategoRolloutBuffer simulator.
+ *
+ * One shared library, libstratego_b200.so, built for sm_100a.  Every entry
+ * point takes plain device pointers, sizes and a cudaStream_t (passed as
+ * void*), launches on that stream and returns 0 on success or a negative
+ * SB_E_* code (sb_last_error() gives the message).  Nothing here allocates
+ * device memory: the caller owns every buffer (the Python host class in
+ * ataraxos_b200/buffer.py allocates them with torch).
+ *
+ * Each entry point replaces one piece of the reference's pybind class
+ * _stratego_cuda.StrategoRolloutBuffer (csrc/stratego_buffer.cpp) or one of
+ * its launchers (csrc/stratego_buffer.cuh); the reference line is cited on
+ * each declaration.  Entry points marked "north-star" have no reference
+ * counterpart: they are the step / setup-pool / sampling / trajectory
+ * contract the build adds around the same state.
+ *
+ * Game state lives in one record of SB_RECORD_BYTES bytes per env (board,
+ * counters, trackers, move-history ring) plus the per-side 64-entry chase
+ * ring (int64 [n,2,64]); sb_export_state() writes it out in the reference's
+ * own tensor layout (csrc/stratego_buffer.cpp:24-55).
+ */
+#ifndef STRATEGO_B200_H
+#define STRATEGO_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SB_ABI_VERSION 1
+#define SB_RECORD_BYTES 256
+#define SB_NUM_SQUARES 100
+#define SB_NUM_ACTIONS 10000
+#define SB_NUM_CHANNELS 488
+#define SB_LIVE_CHANNELS 75      /* channels 0-42 and 456-487 */
+#define SB_COMPACT_CHANNELS 76   /* 0-42, one zero pad plane, 456-487 */
+#define SB_MASK_BITS_BYTES 1250  /* bit j of byte k = flat action 8k+j */
+#define SB_SETUP_BYTES 40        /* one pool entry: piece type per home slot */
+
+/* error codes */
+#define SB_OK 0
+#define SB_E_ARG (-1)      /* bad argument (null pointer, size, alignment) */
+#define SB_E_CUDA (-2)     /* a CUDA runtime call failed */
+#define SB_E_NOPOOL (-3)   /* a pool reset was asked for without a pool */
+
+/* infostate element type and layout */
+#define SB_DTYPE_F32 0
+#define SB_DTYPE_BF16 1
+#define SB_LAYOUT_DENSE_ALL 0  /* [n,488,10,10]; every channel written */
+#define SB_LAYOUT_DENSE_LIVE 1 /* [n,488,10,10]; only channels 0-42, 456-487 written
+                                  (43-455 must already be zero) */
+#define SB_LAYOUT_COMPACT 2    /* [n,76,10,10]; plane 43 is a zero pad that the
+                                  caller zeroes once */
+
+/* action policies for sampling */
+#define SB_POLICY_UNIFORM 0    /* k = (u32 * n_legal) >> 32 over ascending legal actions */
+#define SB_POLICY_GUMBEL 1     /* argmax(logit + Gumbel) over legal actions; logits are
+                                  read from memory when given, else virtual N(0,1) */
+
+/* Device-side state of a shard of envs.  Plain pointers and sizes only. */
+typedef struct sb_state {
+    uint8_t *records;          /* [n, SB_RECORD_BYTES], 16-byte aligned */
+    int64_t *chase_ring;       /* [n, 2, 64] */
+    const int64_t *zobrist;    /* [10,10,2,13] Zobrist table */
+    const uint8_t *setup_pool; /* [pool_size, 40] or NULL */
+    int64_t pool_size;
+    int64_t n;                 /* envs in this shard */
+    int64_t env_base;          /* global index of env 0 (keys the RNG streams) */
+    uint64_t seed;             /* Philox key */
+    int32_t no_attack_limit;   /* draw after this many plies without combat (100) */
+    int32_t max_game_length;   /* draw at this ply count (4000) */
+    int32_t two_square_limit;  /* violation above this many repeats (3) */
+    int32_t reserved;
+    int32_t *status;           /* device word; kernels OR SB_STATUS_* bits in (may be NULL) */
+} sb_state;
+
+#define SB_STATUS_BAD_SETUP 1   /* a setup plane or pool entry held a piece code > 12 */
+
+/* Outputs of one fused step; any pointer may be NULL (not produced). */
+typedef struct sb_step_out {
+    uint8_t *mask_u8;          /* [n,100,100] legal mask of the new state */
+    uint8_t *mask_bits;        /* [n,1250] bit-packed legal mask of the new state */
+    void *infostate;           /* infostate of the new state, see info_dtype/info_layout */
+    int32_t info_dtype;
+    int32_t info_layout;
+    float *reward;             /* [n] reward for player 0 of this transition */
+    uint8_t *done;             /* [n] 1 if the transition ended the game */
+    int64_t *action_taken;     /* [n] action applied this step (-1 none) */
+    float *logprob_taken;      /* [n] log-prob of the applied action when sampled */
+    int16_t *next_action;      /* [n] action proposed for the new state (-1 none) */
+    float *next_logprob;       /* [n] its log-prob */
+    int64_t *hash;             /* [n] Zobrist hash of the new board */
+    int64_t *stats;            /* [5] accumulated over games that ended this step:
+                                  finished, red wins, blue wins, draws, sum of lengths */
+} sb_step_out;
+
+/* Policy / action source of a step. */
+typedef struct sb_policy {
+    int32_t kind;              /* SB_POLICY_* */
+    int32_t reserved;
+    const float *logits;       /* [n,10000] or NULL (virtual Philox N(0,1)) */
+} sb_policy;
+
+/* ---- version / errors ------------------------------------------------ */
+int sb_abi_version(void);
+const char *sb_last_error(void);
+
+/* ---- construction ------------------------------------------------------
+ * Initial state of a fresh buffer: empty board, Red to move, outcome ongoing,
+ * trackers at their reset values (csrc/stratego_buffer.cpp:24-55). */
+int sb_init_state(const sb_state *s, void *stream);
+
+/* hello_world kernel: writes 42 to out[0] (csrc/stratego_buffer.cu:65-76,
+ * csrc/stratego_buffer.cpp:59-67). */
+int sb_hello_world(int32_t *out, void *stream);
+
+/* ---- resets ------------------------------------------------------------
+ * reset_terminated / reset_all from setup planes (csrc/stratego_buffer.cu:529-618,
+ * csrc/stratego_buffer.cpp:245-298): for terminated envs (every env when
+ * force_all != 0) rebuild the board from setup_red/setup_blue [n,10,10] int8
+ * (non-zero = piece, red first), Red to move, trackers cleared, and
+ * flag_captured / terminated_since cleared. */
+int sb_reset_planes(const sb_state *s, const int8_t *setup_red, const int8_t *setup_blue, int force_all,
+                    void *stream);
+
+/* north-star: same reset, with each env's setups drawn from the device setup
+ * pool by Philox(seed; global env index, episode). */
+int sb_reset_pool(const sb_state *s, int force_all, void *stream);
+
+/* north-star: fill pool entries [start, start+count) for `seed`
+ * (Fisher-Yates over the 40-piece roster driven by Philox4x32-10). */
+int sb_make_setup_pool(uint64_t seed, int64_t start, int64_t count, uint8_t *out, void *stream);
+
+/* ---- one ply ------------------------------------------------------------
+ * apply_actions (csrc/stratego_buffer.cu:82-400, csrc/stratego_buffer.cpp:70-120):
+ * validate and apply actions[n] (src*100+dst, int64); illegal actions are
+ * ignored for that env (its invalid counter counts them); flag_captured and
+ * terminated_since updated as the reference's host wrapper does. */
+int sb_apply_actions(const sb_state *s, const int64_t *actions, void *stream);
+
+/* north-star: the fused ply.  actions == NULL samples each env's action at
+ * `ply` with `policy`; then apply, per-env auto-reset from the pool when
+ * auto_reset != 0, then every requested output of the new state, all in one
+ * kernel.  The proposal for the next ply is cached in the record. */
+int sb_step(const sb_state *s, const int64_t *actions, int64_t ply, const sb_policy *policy, int auto_reset,
+            const sb_step_out *out, void *stream);
+
+/* north-star: sample an action for every env's current state at `ply`. */
+int sb_sample_actions(const sb_state *s, int64_t ply, const sb_policy *policy, int64_t *actions, float *logprob,
+                      void *stream);
+
+/* ---- observations of the current state ---------------------------------- */
+/* compute_legal_action_mask (csrc/stratego_buffer.cu:448-523, cpp:123-139):
+ * [n,100,100] uint8 0/1. */
+int sb_legal_mask_u8(const sb_state *s, uint8_t *mask, void *stream);
+/* north-star: bit-packed [n,1250] variant. */
+int sb_legal_mask_bits(const sb_state *s, uint8_t *bits, void *stream);
+/* compute_infostate_tensor (csrc/stratego_buffer.cu:668-797, cpp:154-176). */
+int sb_infostate(const sb_state *s, void *out, int dtype, int layout, void *stream);
+/* hash_board (csrc/stratego_buffer.cu:805-845, cpp:189-203). */
+int sb_hash_board(const sb_state *s, int64_t *out, void *stream);
+/* get_has_legal_movement (csrc/stratego_buffer.cpp:216-219): [n] uint8. */
+int sb_has_legal_movement(const sb_state *s, uint8_t *out, void *stream);
+
+/* Getters of csrc/stratego_buffer.cpp:179-220 and the tracker state, written
+ * in the reference's tensor layout.  Every pointer may be NULL. */
+typedef struct sb_export {
+    int8_t *board_owner;        /* [n,100] */
+    int8_t *board_piece;        /* [n,100] */
+    int8_t *current_player;     /* [n] */
+    int8_t *outcome;            /* [n] */
+    uint8_t *terminated;        /* [n] */
+    uint8_t *flag_captured;     /* [n] */
+    int32_t *move_number;       /* [n] */
+    int32_t *moves_since_attack;/* [n] */
+    int32_t *terminated_since;  /* [n] */
+    uint8_t *moved_squares;     /* [n,100] */
+    uint8_t *revealed_squares;  /* [n,100] */
+    int32_t *move_history;      /* [n,32] */
+    int32_t *move_history_head; /* [n] */
+    int32_t *move_history_len;  /* [n] */
+    int32_t *two_square_count;  /* [n,2] */
+    int32_t *two_square_pair_lo;/* [n,2] */
+    int32_t *two_square_pair_hi;/* [n,2] */
+    uint8_t *two_square_violation; /* [n] */
+    int32_t *chase_hash_head;   /* [n,2] */
+    int32_t *chase_hash_len;    /* [n,2] */
+    int32_t *chase_last_src;    /* [n,2] */
+    uint8_t *chasing_violation; /* [n] */
+    int32_t *episode;           /* [n] */
+    int32_t *invalid_count;     /* [n] */
+    float *reward;              /* [n] compute_reward_pl0 (cpp:142-151) */
+} sb_export;
+
+int sb_export_state(const sb_state *s, const sb_export *out, void *stream);
+
+/* north-star: Σ move_number over envs into *out (current_step, cpp:301-303). */
+int sb_sum_move_number(const sb_state *s, int64_t *out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* STRATEGO_B200_H */

@@ -1,0 +1,324 @@
+"""CPU oracle for the StrategoRolloutBuffer hot path -- TEST INFRASTRUCTURE.
+
+This package is the checker, never the product.  Only ``tests/``,
+``__graft_entry__.smoke()`` and the CPU legs of ``bench.py`` (its
+``cpu_baseline`` and ``--impl reference`` arm) may import it.  The product
+package ``ataraxos_b200`` must never import, link or call anything here.
+
+``stratego_oracle.c`` restates, in plain C, the reference simulator
+(``csrc/stratego_buffer.cu`` / ``.cpp``) and the reference Python engine
+(``stratego/env/rules.py``, ``stratego/env/infostate.py``); every function
+there cites the reference lines it follows.  This module compiles it with
+``gcc`` into ``oracle/_build/`` and exposes :class:`OracleState`, a
+struct-of-arrays state in the reference's own tensor layout
+(``csrc/stratego_buffer.cpp:24-55``) with numpy arrays.
+
+Parity of the oracle is pinned against the golden fixtures in
+``tests/golden/`` (made by running the reference's own Python engine; see
+``tests/golden/make_golden.py``) and against the reference's known-answer
+scenarios ported in ``tests/test_oracle_scenarios.py``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+SRC = HERE / "stratego_oracle.c"
+BUILD_DIR = HERE / "_build"
+LIB_PATH = BUILD_DIR / "libstratego_oracle.so"
+
+NSQ, NACT, NHIST, NRING, NCH = 100, 10000, 32, 64, 488
+POLICY_UNIFORM, POLICY_GUMBEL = 0, 1
+
+
+def build(force: bool = False) -> Path:
+    """Compile the C oracle into ``oracle/_build/`` (gcc, -O2)."""
+    BUILD_DIR.mkdir(exist_ok=True)
+    if force or not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < SRC.stat().st_mtime:
+        tmp = LIB_PATH.with_suffix(f".{os.getpid()}.tmp")
+        subprocess.run(
+            ["gcc", "-O2", "-std=c11", "-Wall", "-shared", "-fPIC", "-o", str(tmp), str(SRC), "-lpthread", "-lm"],
+            check=True,
+        )
+        os.replace(tmp, LIB_PATH)
+    return LIB_PATH
+
+
+class _OState(ctypes.Structure):
+    _fields_ = [
+        ("n", ctypes.c_int64),
+        ("owner", ctypes.c_void_p), ("piece", ctypes.c_void_p),
+        ("moved", ctypes.c_void_p), ("revealed", ctypes.c_void_p),
+        ("current_player", ctypes.c_void_p), ("outcome", ctypes.c_void_p),
+        ("terminated", ctypes.c_void_p), ("flag_captured", ctypes.c_void_p),
+        ("move_number", ctypes.c_void_p), ("moves_since_attack", ctypes.c_void_p),
+        ("terminated_since", ctypes.c_void_p),
+        ("hist", ctypes.c_void_p), ("hist_head", ctypes.c_void_p), ("hist_len", ctypes.c_void_p),
+        ("ts_count", ctypes.c_void_p), ("ts_lo", ctypes.c_void_p), ("ts_hi", ctypes.c_void_p),
+        ("ts_violation", ctypes.c_void_p),
+        ("chase", ctypes.c_void_p), ("chase_head", ctypes.c_void_p), ("chase_len", ctypes.c_void_p),
+        ("chase_last_src", ctypes.c_void_p), ("chase_violation", ctypes.c_void_p),
+        ("episode", ctypes.c_void_p), ("invalid_count", ctypes.c_void_p),
+    ]
+
+
+class _OConfig(ctypes.Structure):
+    _fields_ = [
+        ("zobrist", ctypes.c_void_p),
+        ("no_attack_limit", ctypes.c_int32),
+        ("max_game_length", ctypes.c_int32),
+        ("two_square_limit", ctypes.c_int32),
+        ("pad_", ctypes.c_int32),
+        ("seed", ctypes.c_uint64),
+        ("env_base", ctypes.c_int64),
+        ("pool", ctypes.c_void_p),
+        ("pool_size", ctypes.c_int64),
+    ]
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        _lib = ctypes.CDLL(str(build()))
+        P = ctypes.POINTER
+        vp, i64, i32, u64 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_uint64
+        S, C = P(_OState), P(_OConfig)
+        sig = {
+            "or_philox": (None, [vp, vp, vp]),
+            "or_make_setup": (None, [u64, i64, vp]),
+            "or_make_pool": (None, [u64, i64, i64, vp]),
+            "or_reset_planes": (None, [S, vp, vp, i32]),
+            "or_reset_pool": (None, [S, C, i32]),
+            "or_apply": (None, [S, C, vp]),
+            "or_legal_mask_u8": (None, [S, vp]),
+            "or_legal_mask_bits": (None, [S, vp]),
+            "or_legal_list": (ctypes.c_int, [S, i64, vp]),
+            "or_infostate_f32": (None, [S, C, vp]),
+            "or_infostate_bf16": (None, [S, C, vp]),
+            "or_hash": (None, [S, C, vp]),
+            "or_reward": (None, [S, vp]),
+            "or_sample": (None, [S, C, i64, i32, vp, vp, vp]),
+            "or_step": (None, [S, C, vp, i64, i32, i32, vp, vp, vp, vp]),
+            "or_bench_rollout": (ctypes.c_int, [S, C, i64, i64, i32, vp, vp]),
+            "or_fraction": (ctypes.c_float, [ctypes.c_int32, ctypes.c_int32]),
+            "or_f32_to_bf16": (ctypes.c_uint16, [ctypes.c_float]),
+            "or_logit_noise": (None, [u64, i64, i64, ctypes.c_int32, vp, vp]),
+        }
+        for name, (res, args) in sig.items():
+            f = getattr(_lib, name)
+            f.restype = res
+            f.argtypes = args
+    return _lib
+
+
+def _ptr(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data
+
+
+def philox4x32_10(ctr, key) -> np.ndarray:
+    c = np.ascontiguousarray(ctr, dtype=np.uint32)
+    k = np.ascontiguousarray(key, dtype=np.uint32)
+    out = np.zeros(4, dtype=np.uint32)
+    lib().or_philox(_ptr(c), _ptr(k), _ptr(out))
+    return out
+
+
+def make_setup_pool(seed: int, count: int, start: int = 0) -> np.ndarray:
+    """Pool entries ``[count, 40]`` uint8 (piece type per home-row slot)."""
+    out = np.zeros((count, 40), dtype=np.uint8)
+    lib().or_make_pool(ctypes.c_uint64(seed), start, count, _ptr(out))
+    return out
+
+
+def zobrist_table(seed: int = 42) -> np.ndarray:
+    """The table of ``stratego/env/chasing.py:17-22`` (numpy default_rng)."""
+    rng = np.random.default_rng(seed)
+    return rng.integers(low=0, high=2**63, size=(10, 10, 2, 13), dtype=np.int64)
+
+
+# name -> (dtype, per-env shape, initial value) in the reference layout
+STATE_FIELDS = {
+    "board_owner": (np.int8, (10, 10), -1),
+    "board_piece": (np.int8, (10, 10), 0),
+    "moved_squares": (np.uint8, (NSQ,), 0),
+    "revealed_squares": (np.uint8, (NSQ,), 0),
+    "current_player": (np.int8, (), 0),
+    "outcome": (np.int8, (), -1),
+    "terminated": (np.uint8, (), 0),
+    "flag_captured": (np.uint8, (), 0),
+    "move_number": (np.int32, (), 0),
+    "moves_since_attack": (np.int32, (), 0),
+    "terminated_since": (np.int32, (), 0),
+    "move_history": (np.int32, (NHIST,), 0),
+    "move_history_head": (np.int32, (), 0),
+    "move_history_len": (np.int32, (), 0),
+    "two_square_count": (np.int32, (2,), 0),
+    "two_square_pair_lo": (np.int32, (2,), -1),
+    "two_square_pair_hi": (np.int32, (2,), -1),
+    "two_square_violation": (np.uint8, (), 0),
+    "chase_hashes": (np.int64, (2, NRING), 0),
+    "chase_hash_head": (np.int32, (2,), 0),
+    "chase_hash_len": (np.int32, (2,), 0),
+    "chase_last_src": (np.int32, (2,), -1),
+    "chasing_violation": (np.uint8, (), 0),
+    "episode": (np.int32, (), 0),
+    "invalid_count": (np.int32, (), 0),
+}
+
+_CFIELD = {
+    "board_owner": "owner", "board_piece": "piece", "moved_squares": "moved", "revealed_squares": "revealed",
+    "current_player": "current_player", "outcome": "outcome", "terminated": "terminated",
+    "flag_captured": "flag_captured", "move_number": "move_number", "moves_since_attack": "moves_since_attack",
+    "terminated_since": "terminated_since", "move_history": "hist", "move_history_head": "hist_head",
+    "move_history_len": "hist_len", "two_square_count": "ts_count", "two_square_pair_lo": "ts_lo",
+    "two_square_pair_hi": "ts_hi", "two_square_violation": "ts_violation", "chase_hashes": "chase",
+    "chase_hash_head": "chase_head", "chase_hash_len": "chase_len", "chase_last_src": "chase_last_src",
+    "chasing_violation": "chase_violation", "episode": "episode", "invalid_count": "invalid_count",
+}
+
+
+class OracleState:
+    """N independent games on the CPU, reference tensor layout, numpy arrays."""
+
+    def __init__(
+        self,
+        n: int,
+        *,
+        seed: int = 0,
+        env_base: int = 0,
+        no_attack_limit: int = 100,
+        max_game_length: int = 4000,
+        two_square_limit: int = 3,
+        zobrist: np.ndarray | None = None,
+        pool: np.ndarray | None = None,
+    ) -> None:
+        self.n = int(n)
+        self.a: dict[str, np.ndarray] = {}
+        for name, (dt, shp, init) in STATE_FIELDS.items():
+            self.a[name] = np.full((self.n, *shp), init, dtype=dt)
+        self._st = _OState(n=self.n, **{_CFIELD[k]: _ptr(v) for k, v in self.a.items()})
+        self.zobrist = np.ascontiguousarray(zobrist_table() if zobrist is None else zobrist, dtype=np.int64)
+        self.pool = None if pool is None else np.ascontiguousarray(pool, dtype=np.uint8)
+        self._cfg = _OConfig(
+            zobrist=_ptr(self.zobrist),
+            no_attack_limit=no_attack_limit,
+            max_game_length=max_game_length,
+            two_square_limit=two_square_limit,
+            seed=seed,
+            env_base=env_base,
+            pool=_ptr(self.pool),
+            pool_size=0 if self.pool is None else len(self.pool),
+        )
+        self.ply = 0
+
+    # -- state -----------------------------------------------------------
+    def export(self) -> dict[str, np.ndarray]:
+        return {k: v.copy() for k, v in self.a.items()}
+
+    # -- reference API ---------------------------------------------------
+    def reset_planes(self, setup_red: np.ndarray, setup_blue: np.ndarray, force_all: bool = False) -> None:
+        r = np.ascontiguousarray(setup_red, dtype=np.int8).reshape(self.n, NSQ)
+        b = np.ascontiguousarray(setup_blue, dtype=np.int8).reshape(self.n, NSQ)
+        lib().or_reset_planes(ctypes.byref(self._st), _ptr(r), _ptr(b), int(force_all))
+
+    def reset_pool(self, force_all: bool = False) -> None:
+        assert self.pool is not None, "no setup pool"
+        lib().or_reset_pool(ctypes.byref(self._st), ctypes.byref(self._cfg), int(force_all))
+
+    def apply(self, actions) -> None:
+        a = np.ascontiguousarray(actions, dtype=np.int64).reshape(self.n)
+        lib().or_apply(ctypes.byref(self._st), ctypes.byref(self._cfg), _ptr(a))
+        self.ply += 1
+
+    def legal_mask_u8(self) -> np.ndarray:
+        out = np.empty((self.n, NSQ, NSQ), dtype=np.uint8)
+        lib().or_legal_mask_u8(ctypes.byref(self._st), _ptr(out))
+        return out
+
+    def legal_mask_bits(self) -> np.ndarray:
+        out = np.empty((self.n, NACT // 8), dtype=np.uint8)
+        lib().or_legal_mask_bits(ctypes.byref(self._st), _ptr(out))
+        return out
+
+    def legal_list(self, g: int) -> np.ndarray:
+        out = np.empty(NACT, dtype=np.int16)
+        k = lib().or_legal_list(ctypes.byref(self._st), g, _ptr(out))
+        return out[:k].astype(np.int64)
+
+    def infostate_f32(self) -> np.ndarray:
+        out = np.empty((self.n, NCH, 10, 10), dtype=np.float32)
+        lib().or_infostate_f32(ctypes.byref(self._st), ctypes.byref(self._cfg), _ptr(out))
+        return out
+
+    def infostate_bf16_bits(self) -> np.ndarray:
+        """bfloat16 planes as their uint16 bit patterns ``[n,488,10,10]``."""
+        out = np.empty((self.n, NCH, 10, 10), dtype=np.uint16)
+        lib().or_infostate_bf16(ctypes.byref(self._st), ctypes.byref(self._cfg), _ptr(out))
+        return out
+
+    def hash_board(self) -> np.ndarray:
+        out = np.empty(self.n, dtype=np.int64)
+        lib().or_hash(ctypes.byref(self._st), ctypes.byref(self._cfg), _ptr(out))
+        return out
+
+    def reward_pl0(self) -> np.ndarray:
+        out = np.empty(self.n, dtype=np.float32)
+        lib().or_reward(ctypes.byref(self._st), _ptr(out))
+        return out
+
+    # -- north-star additions ----------------------------------------------
+    def sample(self, ply: int | None = None, policy: int = POLICY_UNIFORM):
+        ply = self.ply if ply is None else ply
+        acts = np.empty(self.n, dtype=np.int64)
+        lp = np.empty(self.n, dtype=np.float32)
+        nl = np.empty(self.n, dtype=np.int32)
+        lib().or_sample(ctypes.byref(self._st), ctypes.byref(self._cfg), ply, policy, _ptr(acts), _ptr(lp), _ptr(nl))
+        return acts, lp, nl
+
+    def step(self, actions=None, *, policy: int = POLICY_UNIFORM, auto_reset: bool = True) -> dict[str, np.ndarray]:
+        a = None if actions is None else np.ascontiguousarray(actions, dtype=np.int64).reshape(self.n)
+        taken = np.empty(self.n, dtype=np.int64)
+        lp = np.empty(self.n, dtype=np.float32)
+        rew = np.empty(self.n, dtype=np.float32)
+        done = np.empty(self.n, dtype=np.uint8)
+        lib().or_step(
+            ctypes.byref(self._st), ctypes.byref(self._cfg), _ptr(a), self.ply, policy, int(auto_reset),
+            _ptr(taken), _ptr(lp), _ptr(rew), _ptr(done),
+        )
+        self.ply += 1
+        return {"action": taken, "logprob": lp, "reward": rew, "done": done}
+
+    def bench_rollout(self, plies: int, threads: int) -> None:
+        """Uniform random rollout with u8 mask + bf16 dense infostate outputs."""
+        mask = np.empty((self.n, NACT), dtype=np.uint8)
+        info = np.empty((self.n, NCH * NSQ), dtype=np.uint16)
+        rc = lib().or_bench_rollout(
+            ctypes.byref(self._st), ctypes.byref(self._cfg), plies, self.ply, threads, _ptr(mask), _ptr(info)
+        )
+        if rc != 0:
+            raise RuntimeError("oracle bench rollout failed to start its threads")
+        self.ply += plies
+
+
+def fraction(num: int, den: int) -> float:
+    return float(lib().or_fraction(num, den))
+
+
+def f32_to_bf16_bits(x: float) -> int:
+    return int(lib().or_f32_to_bf16(x))
+
+
+def logit_noise(seed: int, genv: int, ply: int, action: int) -> tuple[float, float]:
+    z = ctypes.c_float()
+    g = ctypes.c_float()
+    lib().or_logit_noise(ctypes.c_uint64(seed), genv, ply, action, ctypes.addressof(z), ctypes.addressof(g))
+    return z.value, g.value
