@@ -72,7 +72,7 @@ struct KArgs {
     int64_t* stats;
     int64_t* sampled;
     float* sampled_lp;
-    int32_t sm_warp, sm_r1, sm_hist, sm_mask, sm_bits;
+    int32_t sm_warp;
 };
 
 constexpr int WARPS = 4;  // warps (envs in flight) per CTA
@@ -182,6 +182,7 @@ __device__ __forceinline__ void logit_noise(uint64_t seed, int64_t ge, int64_t p
 // Choose an action for the current state (rays/cnt already enumerated).
 // Uniform: k = (u32 * n) >> 32 over ascending legal actions.  Gumbel: argmax
 // of logit + Gumbel over legal actions, ties to the smaller action index.
+template <int POL>
 __device__ void choose(const KArgs& a, const uint16_t* rays, const int cnt[4], int n, int64_t e, int64_t ply,
                        int lane, int& act, float& lp) {
     const int64_t ge = a.env_base + e;
@@ -190,7 +191,8 @@ __device__ void choose(const KArgs& a, const uint16_t* rays, const int cnt[4], i
         lp = 0.0f;
         return;
     }
-    if (a.policy == SB_POLICY_UNIFORM) {
+    const int pol = POL >= 0 ? POL : a.policy;
+    if (pol == SB_POLICY_UNIFORM) {
         const uint4 w = philox((uint32_t)ge, (uint32_t)ply, (uint32_t)((uint64_t)ply >> 32), TAG_ACTION, a.seed);
         act = kth_action((int)mulshift(w.x, (uint32_t)n), cnt, rays, lane);
         lp = -logf((float)n);
@@ -336,8 +338,10 @@ __device__ void reset_env(uint8_t* rec, int64_t* ring2, const KArgs& a, int64_t 
 // success the board, counters, history, trackers and the caps part of the
 // terminal check are done; check_legal asks the caller for the "side to move
 // has no legal move" test on the new board.
-__device__ bool apply_env(uint8_t* rec, int64_t* ring2, const KArgs& a, int64_t act, int lane, bool& check_legal,
-                          bool& flag_taken) {
+// ring_lo / ring_hi: this lane's prefetched entries lane and lane+32 of the
+// mover's chase ring (valid below the ring length).
+__device__ bool apply_env(uint8_t* rec, int64_t* ring2, const KArgs& a, int64_t act, int lane, uint64_t ring_lo,
+                          uint64_t ring_hi, bool& check_legal, bool& flag_taken) {
     check_legal = false;
     flag_taken = false;
     if (act < 0 || act >= NACT) return false;
@@ -433,9 +437,7 @@ __device__ bool apply_env(uint8_t* rec, int64_t* ring2, const KArgs& a, int64_t 
     uint8_t chv = rec[R_CHVIOL];
     int64_t* ring = ring2 + p * NRING;
     if (threat) {
-        bool f = false;
-        if (lane < chl) f = (uint64_t)ring[lane] == h;
-        if (lane + 32 < chl) f = f || (uint64_t)ring[lane + 32] == h;
+        const bool f = (lane < chl && ring_lo == h) || (lane + 32 < chl && ring_hi == h);
         const bool found = __any_sync(FULL, f);
         const bool exc = chlast >= 0 && dst == chlast;
         if (found && !exc) chv = 1;
@@ -484,8 +486,14 @@ __device__ bool apply_env(uint8_t* rec, int64_t* ring2, const KArgs& a, int64_t 
 }
 
 // ---------------------------------------------------------------------------
-// Observation staging
+// Observations, written straight from registers
 // ---------------------------------------------------------------------------
+//
+// Every output row of an env is contiguous, so each lane writes whole 16-byte
+// chunks of its background (zeros, the hidden-piece 1/12 patterns, the two
+// constant planes) and, after a __syncwarp that orders the warp's stores, the
+// few one-hot values land on top as 1-, 2- or 4-byte stores.  The L2 merges
+// the partial sectors, so HBM sees each output byte written once.
 
 template <typename T>
 struct IV;
@@ -504,24 +512,37 @@ union Chunk {
     T e[16 / sizeof(T)];
 };
 
-// Infostate of the side to move (stratego/env/infostate.py:37-109, channel
-// meaning as csrc/stratego_buffer.cu:707-767) into the region-1 staging
-// buffer (channels 0-42, padded to 16 bytes) and the history staging buffer
-// (channels 456-487).
+__device__ __forceinline__ void st16(void* p, uint4 v) { *reinterpret_cast<uint4*>(p) = v; }
+
 template <typename T>
-__device__ void stage_infostate(const uint8_t* rec, const KArgs& a, int lane, T* r1, T* hs, T* pat_opp, T* pat_own) {
-    constexpr int PB = NSQ * (int)sizeof(T);
-    constexpr int R1B = ((43 * PB + 15) / 16) * 16;
-    constexpr int HB = 32 * PB;
+struct InfoGeom {
+    static constexpr int PB = NSQ * (int)sizeof(T);          // bytes per plane
+    static constexpr int R1B = ((43 * PB + 15) / 16) * 16;   // channels 0-42, padded
+    static constexpr int HB = 32 * PB;                        // channels 456-487
+};
+
+__device__ __forceinline__ void zero_chunks(uint8_t* g, int nchunks, int lane) {
+    const uint4 Z = make_uint4(0, 0, 0, 0);
+    for (int i = lane; i < nchunks; i += 32) st16(g + i * 16, Z);
+}
+
+// Background of the infostate (stratego/env/infostate.py:37-109): the rows
+// of hidden-piece probabilities (channels 12-23 opponent, 24-35 own), the
+// constant planes 41/42, zeros elsewhere; channels 456-487 zeroed.  The
+// 400-byte hidden-piece row (two bf16 planes or one f32 plane) is built in
+// shared memory and lanes 0-24 each replicate one 16-byte column of it.
+template <typename T>
+__device__ void info_background(const uint8_t* rec, const KArgs& a, int lane, uint8_t* g, int hist_off, bool all,
+                                T* pat_opp, T* pat_own) {
+    using G = InfoGeom<T>;
+    constexpr int PB = G::PB;
+    constexpr int REPS = 12 * PB / 400;
+    constexpr int C41 = 41 * PB / 16;  // first chunk touching plane 41
     const int p = rec[R_PLAYER];
-    const T ONE = IV<T>::from(1.0f), NEG = IV<T>::from(-1.0f), TW = IV<T>::from(__fdiv_rn(1.0f, 12.0f));
-    const T ZERO = IV<T>::from(0.0f);
-    // hidden-piece rows for channels 12-23 (opponent) and 24-35 (own);
-    // one period = 400 bytes (two bf16 planes or one f32 plane)
-#pragma unroll
+    const T TW = IV<T>::from(__fdiv_rn(1.0f, 12.0f)), ZERO = IV<T>::from(0.0f);
     for (int k = 0; k < 4; ++k) {
         const int sq = lane + 32 * k;
-        if (sq >= NSQ) continue;
+        if (sq >= NSQ) break;
         const uint8_t c = rec[sq];
         const bool occ = c & C_OCC, rev = c & C_REV;
         const bool own = occ && ((c >> 4) & 1) == p, opp = occ && !own;
@@ -534,31 +555,41 @@ __device__ void stage_infostate(const uint8_t* rec, const KArgs& a, int lane, T*
         }
     }
     __syncwarp();
+    if (lane < 25) {
+        const uint4 vo = reinterpret_cast<const uint4*>(pat_opp)[lane];
+        const uint4 vw = reinterpret_cast<const uint4*>(pat_own)[lane];
+        uint8_t* go = g + 12 * PB + lane * 16;
+        uint8_t* gw = g + 24 * PB + lane * 16;
+#pragma unroll
+        for (int r = 0; r < REPS; ++r) {
+            st16(go + r * 400, vo);
+            st16(gw + r * 400, vw);
+        }
+    }
+    zero_chunks(g, 12 * PB / 16, lane);
+    zero_chunks(g + 36 * PB, C41 - 36 * PB / 16, lane);
     const int mn = fld<int32_t>(rec, R_MOVENUM), msa = fld<int32_t>(rec, R_MSA);
     const T v41 = IV<T>::from(a.max_len > 0 ? __fdiv_rn((float)mn, (float)a.max_len) : 0.0f);
     const T v42 = IV<T>::from(a.no_attack_limit > 0 ? __fdiv_rn((float)msa, (float)a.no_attack_limit) : 0.0f);
-    uint8_t* r1b = reinterpret_cast<uint8_t*>(r1);
-    for (int i = lane; i < R1B / 16; i += 32) {
-        const int off = i * 16;
+    for (int i = C41 + lane; i < G::R1B / 16; i += 32) {
         Chunk<T> ch;
-        if (off >= 12 * PB && off < 36 * PB) {
-            const bool o = off < 24 * PB;
-            const uint8_t* row = reinterpret_cast<const uint8_t*>(o ? pat_opp : pat_own);
-            ch.v = *reinterpret_cast<const uint4*>(row + (off - (o ? 12 : 24) * PB) % 400);
-        } else if (off + 16 > 41 * PB && off < 43 * PB) {
 #pragma unroll
-            for (int j = 0; j < 16 / (int)sizeof(T); ++j) {
-                const int pl = (off + j * (int)sizeof(T)) / PB;
-                ch.e[j] = pl == 41 ? v41 : (pl == 42 ? v42 : ZERO);
-            }
-        } else {
-            ch.v = make_uint4(0, 0, 0, 0);
+        for (int j = 0; j < 16 / (int)sizeof(T); ++j) {
+            const int pl = (i * 16 + j * (int)sizeof(T)) / PB;
+            ch.e[j] = pl == 41 ? v41 : (pl == 42 ? v42 : ZERO);
         }
-        *reinterpret_cast<uint4*>(r1b + off) = ch.v;
+        st16(g + i * 16, ch.v);
     }
-    uint8_t* hsb = reinterpret_cast<uint8_t*>(hs);
-    for (int i = lane; i < HB / 16; i += 32) *reinterpret_cast<uint4*>(hsb + i * 16) = make_uint4(0, 0, 0, 0);
-    __syncwarp();
+    zero_chunks(g + hist_off, G::HB / 16, lane);
+    if (all) zero_chunks(g + G::R1B, (456 * PB - G::R1B) / 16, lane);
+}
+
+// One-hot values of channels 0-11, 24-40 and the +1/-1 of 456-487.
+template <typename T>
+__device__ void info_scatter(const uint8_t* rec, int lane, uint8_t* g, int hist_off) {
+    const int p = rec[R_PLAYER];
+    const T ONE = IV<T>::from(1.0f), NEG = IV<T>::from(-1.0f);
+    T* r1 = reinterpret_cast<T*>(g);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int sq = lane + 32 * k;
@@ -579,6 +610,7 @@ __device__ void stage_infostate(const uint8_t* rec, const KArgs& a, int lane, T*
     }
     const int hl = rec[R_HLEN], hh = rec[R_HHEAD];
     if (lane < hl) {
+        T* hs = reinterpret_cast<T*>(g + hist_off);
         const int slot = (hh - 1 - lane) & 31;
         const int act = fld<int16_t>(rec, R_HIST + 2 * slot);
         hs[lane * NSQ + act % 100] = ONE;
@@ -586,11 +618,10 @@ __device__ void stage_infostate(const uint8_t* rec, const KArgs& a, int lane, T*
     }
 }
 
-// u8 legal mask of the side to move (csrc/stratego_buffer.cu:448-507) from
-// the packed rays into a zeroed 10,000-byte staging buffer.
-__device__ void stage_mask_u8(const uint16_t* rays, int lane, uint8_t* m) {
-    for (int i = lane; i < NACT / 16; i += 32) reinterpret_cast<uint4*>(m)[i] = make_uint4(0, 0, 0, 0);
-    __syncwarp();
+// u8 legal mask (csrc/stratego_buffer.cu:448-507): zero rows, then ones.
+__device__ __forceinline__ void mask_background(uint8_t* g, int lane) { zero_chunks(g, NACT / 16, lane); }
+
+__device__ void mask_scatter(const uint16_t* rays, int lane, uint8_t* m) {
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int sq = lane + 32 * k;
@@ -606,8 +637,8 @@ __device__ void stage_mask_u8(const uint16_t* rays, int lane, uint8_t* m) {
     }
 }
 
-// bit-packed mask: bit j of byte k = flat action 8k+j.
-__device__ void stage_mask_bits(const uint16_t* rays, int lane, uint32_t* w) {
+// bit-packed mask: bit j of byte k = flat action 8k+j, built in shared memory.
+__device__ void mask_bits(const uint16_t* rays, int lane, uint32_t* w, uint8_t* g) {
     for (int i = lane; i < 79; i += 32) reinterpret_cast<uint4*>(w)[i] = make_uint4(0, 0, 0, 0);
     __syncwarp();
 #pragma unroll
@@ -616,49 +647,76 @@ __device__ void stage_mask_bits(const uint16_t* rays, int lane, uint32_t* w) {
         if (sq >= NSQ) continue;
         const uint32_t r = rays[sq];
         if (!r) continue;
-        const int up = r & 15, left = (r >> 4) & 15, right = (r >> 8) & 15, down = r >> 12;
-        const int n = up + left + right + down;
+        const int n = (r & 15) + ((r >> 4) & 15) + ((r >> 8) & 15) + (r >> 12);
         for (int j = 0; j < n; ++j) {
             const int f = sq * 100 + decode_ray(sq, r, j);
             atomicOr(&w[f >> 5], 1u << (f & 31));
         }
     }
+    __syncwarp();
+    const uint16_t* src = reinterpret_cast<const uint16_t*>(w);
+    uint16_t* dst = reinterpret_cast<uint16_t*>(g);
+    for (int i = lane; i < SB_MASK_BITS_BYTES / 2; i += 32) dst[i] = src[i];
 }
 
 // ---------------------------------------------------------------------------
 // The per-env kernel
 // ---------------------------------------------------------------------------
 
-template <typename T>
-__global__ void __launch_bounds__(WARPS * 32) env_kernel(const KArgs a) {
+// Shared memory per warp: record (256), rays (256), two hidden-piece rows
+// (2 x 400) and, for bit-packed masks only, a 1264-byte bit buffer.
+constexpr int SM_BITS = SM_FIXED;
+
+// MODE: MODE_GENERIC takes every decision from a.flags; the step modes fix
+// apply + step + propose (and the policy) at compile time so that the hot
+// kernel carries only the code it runs.
+constexpr int MODE_GENERIC = 0, MODE_STEP_UNIFORM = 1, MODE_STEP_GUMBEL = 2;
+
+template <typename T, int MODE>
+__global__ void __launch_bounds__(WARPS * 32, 8) env_kernel(const KArgs a) {
+    constexpr bool kStep = MODE != MODE_GENERIC;
+    constexpr int kPol = MODE == MODE_STEP_UNIFORM ? SB_POLICY_UNIFORM : (MODE == MODE_STEP_GUMBEL ? SB_POLICY_GUMBEL : -1);
+    auto has = [&](uint32_t f) -> bool {
+        if (kStep) {
+            if (f & (F_RESET_PLANES | F_RESET_POOL | F_SAMPLE_OUT | F_HAS_LEGAL)) return false;
+            if (f & (F_APPLY | F_STEP | F_PROPOSE)) return true;
+        }
+        return (a.flags & f) != 0;
+    };
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31;
     uint8_t* ws = smem + (threadIdx.x >> 5) * a.sm_warp;
     uint8_t* rec = ws;
     uint16_t* rays = reinterpret_cast<uint16_t*>(ws + SM_RAYS);
-    bool staged = false;
     const int64_t nwarps = (int64_t)gridDim.x * WARPS;
     for (int64_t e = (int64_t)blockIdx.x * WARPS + (threadIdx.x >> 5); e < a.n; e += nwarps) {
         reinterpret_cast<uint2*>(rec)[lane] = reinterpret_cast<const uint2*>(a.rec + e * REC)[lane];
         __syncwarp();
         int64_t* ring2 = a.ring + e * 2 * NRING;
         bool dirty = false;
-        int cnt[4];
+        bool rays_ok = false;  // rays/cnt describe the side to move of the current board
+        int cnt[4] = {0, 0, 0, 0};
 
-        if ((a.flags & (F_RESET_PLANES | F_RESET_POOL)) && ((a.flags & F_FORCE) || rec[R_TERM])) {
-            reset_env(rec, ring2, a, e, (a.flags & F_RESET_POOL) != 0, lane);
+        if ((has(F_RESET_PLANES) || has(F_RESET_POOL)) && (has(F_FORCE) || rec[R_TERM])) {
+            reset_env(rec, ring2, a, e, has(F_RESET_POOL), lane);
             dirty = true;
         }
 
-        if (a.flags & F_APPLY) {
+        if (has(F_APPLY)) {
             const bool was_term = rec[R_TERM] != 0;
             int64_t act = -1;
             float lp = 0.0f;
             if (!was_term) {
+                // the mover's chase ring, fetched early (used on threatening moves)
+                const int pm = rec[R_PLAYER];
+                const int rl = rec[R_CHLEN + pm];
+                const int64_t* ringm = ring2 + pm * NRING;
+                const uint64_t ring_lo = lane < rl ? (uint64_t)ringm[lane] : 0;
+                const uint64_t ring_hi = lane + 32 < rl ? (uint64_t)ringm[lane + 32] : 0;
                 int n_legal = -1;
                 if (a.actions) act = a.actions[e];
-                if (!a.actions || (a.flags & F_STEP)) {
-                    if (fld<int32_t>(rec, R_PROPPLY) == (int32_t)a.ply && rec[R_PROPKIND] == a.policy &&
+                if (!a.actions || has(F_STEP)) {
+                    if (fld<int32_t>(rec, R_PROPPLY) == (int32_t)a.ply && rec[R_PROPKIND] == (kPol >= 0 ? kPol : a.policy) &&
                         !a.logits) {
                         n_legal = fld<int16_t>(rec, R_NLEGAL);
                         if (!a.actions) {
@@ -666,20 +724,20 @@ __global__ void __launch_bounds__(WARPS * 32) env_kernel(const KArgs a) {
                             lp = fld<float>(rec, R_PROPLP);
                         }
                     } else {
-                        enumerate(rec, rec[R_PLAYER], rays, lane, cnt);
+                        enumerate(rec, pm, rays, lane, cnt);
                         n_legal = count_of(cnt);
                         if (!a.actions) {
                             int ac;
-                            choose(a, rays, cnt, n_legal, e, a.ply, lane, ac, lp);
+                            choose<kPol>(a, rays, cnt, n_legal, e, a.ply, lane, ac, lp);
                             act = ac;
                         }
                     }
                 }
-                if ((a.flags & F_STEP) && n_legal == 0) {
+                if (has(F_STEP) && n_legal == 0) {
                     // a start position whose side to move cannot move: it
                     // loses (the rule of stratego/env/rules.py:406-413)
                     if (lane == 0) {
-                        fld<int8_t>(rec, R_OUTCOME) = (int8_t)(rec[R_PLAYER] == 0 ? 1 : 0);
+                        fld<int8_t>(rec, R_OUTCOME) = (int8_t)(pm == 0 ? 1 : 0);
                         rec[R_TERM] = 1;
                         fld<int32_t>(rec, R_PROPPLY) = -1;
                     }
@@ -687,17 +745,21 @@ __global__ void __launch_bounds__(WARPS * 32) env_kernel(const KArgs a) {
                     __syncwarp();
                 } else {
                     bool chk, flag;
-                    const bool ok = apply_env(rec, ring2, a, act, lane, chk, flag);
+                    const bool ok = apply_env(rec, ring2, a, act, lane, ring_lo, ring_hi, chk, flag);
                     if (!ok) {
                         if (lane == 0) fld<int32_t>(rec, R_INVALID) += 1;
+                        __syncwarp();
                     } else if (chk) {
                         enumerate(rec, rec[R_PLAYER], rays, lane, cnt);
-                        if (count_of(cnt) == 0 && lane == 0) {
-                            fld<int8_t>(rec, R_OUTCOME) = (int8_t)(rec[R_PLAYER] == 0 ? 1 : 0);
-                            rec[R_TERM] = 1;
+                        rays_ok = true;
+                        if (count_of(cnt) == 0) {
+                            if (lane == 0) {
+                                fld<int8_t>(rec, R_OUTCOME) = (int8_t)(rec[R_PLAYER] == 0 ? 1 : 0);
+                                rec[R_TERM] = 1;
+                            }
+                            __syncwarp();
                         }
                     }
-                    __syncwarp();
                 }
             }
             const bool term = rec[R_TERM] != 0;
@@ -717,89 +779,65 @@ __global__ void __launch_bounds__(WARPS * 32) env_kernel(const KArgs a) {
             }
             __syncwarp();
             dirty = true;
-            if ((a.flags & F_AUTO_RESET) && term) reset_env(rec, ring2, a, e, true, lane);
+            if (has(F_AUTO_RESET) && term) {
+                reset_env(rec, ring2, a, e, true, lane);
+                rays_ok = false;
+            }
         }
 
-        const bool observe = (a.flags & (F_MASK_U8 | F_MASK_BITS | F_PROPOSE | F_HAS_LEGAL | F_SAMPLE_OUT)) != 0;
+        const bool observe = has(F_MASK_U8) || has(F_MASK_BITS) || has(F_PROPOSE) || has(F_HAS_LEGAL) || has(F_SAMPLE_OUT);
+        int n = 0;
         if (observe) {
-            enumerate(rec, rec[R_PLAYER], rays, lane, cnt);
-            const int n = count_of(cnt);
-            __syncwarp();
-            if (a.flags & (F_PROPOSE | F_SAMPLE_OUT)) {
-                const int64_t pp = (a.flags & F_PROPOSE) ? a.propose_ply : a.ply;
-                int ac;
-                float lp;
-                choose(a, rays, cnt, n, e, pp, lane, ac, lp);
-                if (lane == 0) {
-                    if (a.flags & F_PROPOSE) {
-                        fld<int16_t>(rec, R_PROP) = (int16_t)ac;
-                        fld<int32_t>(rec, R_PROPPLY) = a.logits ? -1 : (int32_t)pp;
-                        rec[R_PROPKIND] = (uint8_t)a.policy;
-                        fld<int16_t>(rec, R_NLEGAL) = (int16_t)n;
-                        fld<float>(rec, R_PROPLP) = lp;
-                        if (a.next_action) a.next_action[e] = (int16_t)ac;
-                        if (a.next_logprob) a.next_logprob[e] = lp;
-                    }
-                    if (a.flags & F_SAMPLE_OUT) {
-                        if (a.sampled) a.sampled[e] = ac;
-                        if (a.sampled_lp) a.sampled_lp[e] = lp;
-                    }
-                }
-                if (a.flags & F_PROPOSE) dirty = true;
-            }
-            if ((a.flags & F_HAS_LEGAL) && lane == 0) a.has_legal[e] = n > 0;
+            if (!rays_ok) enumerate(rec, rec[R_PLAYER], rays, lane, cnt);
+            n = count_of(cnt);
         }
-        if ((a.flags & F_HASH) && lane == 0) a.hash[e] = fld<int64_t>(rec, R_ZHASH);
-
-        if (a.flags & (F_MASK_U8 | F_MASK_BITS | F_INFO)) {
-            if (staged && lane == 0) bulk_wait_read();
-            __syncwarp();
-            bool issue = false;
-            if (a.flags & F_MASK_U8) {
-                stage_mask_u8(rays, lane, ws + a.sm_mask);
-                issue = true;
-            }
-            if (a.flags & F_MASK_BITS) stage_mask_bits(rays, lane, reinterpret_cast<uint32_t*>(ws + a.sm_bits));
-            if (a.flags & F_INFO) {
-                stage_infostate<T>(rec, a, lane, reinterpret_cast<T*>(ws + a.sm_r1), reinterpret_cast<T*>(ws + a.sm_hist),
-                                   reinterpret_cast<T*>(ws + SM_PAT_OPP), reinterpret_cast<T*>(ws + SM_PAT_OWN));
-                issue = true;
-            }
-            fence_async_smem();
-            __syncwarp();
-            if (a.flags & F_MASK_BITS) {
-                const uint16_t* src = reinterpret_cast<const uint16_t*>(ws + a.sm_bits);
-                uint16_t* dst = reinterpret_cast<uint16_t*>(a.mask_bits + e * SB_MASK_BITS_BYTES);
-                for (int i = lane; i < SB_MASK_BITS_BYTES / 2; i += 32) dst[i] = src[i];
-            }
-            if (a.flags & F_INFO) {
-                constexpr int PB = NSQ * (int)sizeof(T);
-                constexpr int R1B = ((43 * PB + 15) / 16) * 16;
-                const bool compact = a.info_layout == SB_LAYOUT_COMPACT;
-                uint8_t* base = reinterpret_cast<uint8_t*>(a.info) + e * (int64_t)(compact ? 76 : NCH) * PB;
-                if (a.info_layout == SB_LAYOUT_DENSE_ALL) {
-                    for (int i = R1B / 16 + lane; i < 456 * PB / 16; i += 32)
-                        reinterpret_cast<uint4*>(base)[i] = make_uint4(0, 0, 0, 0);
-                }
-                if (lane == 0) {
-                    bulk_s2g(base, ws + a.sm_r1, R1B);
-                    bulk_s2g(base + (compact ? 44 : 456) * PB, ws + a.sm_hist, 32 * PB);
-                }
-            }
-            if ((a.flags & F_MASK_U8) && lane == 0) bulk_s2g(a.mask_u8 + e * NACT, ws + a.sm_mask, NACT);
-            if (issue) {
-                if (lane == 0) bulk_commit();
-                staged = true;
-            }
+        // background rows of the outputs, then (after one __syncwarp) the one-hots
+        uint8_t* ginfo = nullptr;
+        int hist_off = 0;
+        if (has(F_INFO)) {
+            constexpr int PB = InfoGeom<T>::PB;
+            const bool compact = a.info_layout == SB_LAYOUT_COMPACT;
+            ginfo = reinterpret_cast<uint8_t*>(a.info) + e * (int64_t)(compact ? 76 : NCH) * PB;
+            hist_off = (compact ? 44 : 456) * PB;
+            info_background<T>(rec, a, lane, ginfo, hist_off, a.info_layout == SB_LAYOUT_DENSE_ALL,
+                               reinterpret_cast<T*>(ws + SM_PAT_OPP), reinterpret_cast<T*>(ws + SM_PAT_OWN));
         }
-
-        if (dirty) {
-            __syncwarp();
-            reinterpret_cast<uint2*>(a.rec + e * REC)[lane] = reinterpret_cast<const uint2*>(rec)[lane];
+        if (has(F_MASK_U8)) mask_background(a.mask_u8 + e * NACT, lane);
+        if (has(F_PROPOSE) || has(F_SAMPLE_OUT)) {
+            const int64_t pp = has(F_PROPOSE) ? a.propose_ply : a.ply;
+            int ac;
+            float lp;
+            choose<kPol>(a, rays, cnt, n, e, pp, lane, ac, lp);
+            if (lane == 0) {
+                if (has(F_PROPOSE)) {
+                    fld<int16_t>(rec, R_PROP) = (int16_t)ac;
+                    fld<int32_t>(rec, R_PROPPLY) = a.logits ? -1 : (int32_t)pp;
+                    rec[R_PROPKIND] = (uint8_t)(kPol >= 0 ? kPol : a.policy);
+                    fld<int16_t>(rec, R_NLEGAL) = (int16_t)n;
+                    fld<float>(rec, R_PROPLP) = lp;
+                    if (a.next_action) a.next_action[e] = (int16_t)ac;
+                    if (a.next_logprob) a.next_logprob[e] = lp;
+                }
+                if (has(F_SAMPLE_OUT)) {
+                    if (a.sampled) a.sampled[e] = ac;
+                    if (a.sampled_lp) a.sampled_lp[e] = lp;
+                }
+            }
+            if (has(F_PROPOSE)) dirty = true;
+        }
+        if (lane == 0) {
+            if (has(F_HAS_LEGAL)) a.has_legal[e] = n > 0;
+            if (has(F_HASH)) a.hash[e] = fld<int64_t>(rec, R_ZHASH);
         }
         __syncwarp();
+        if (has(F_MASK_U8)) mask_scatter(rays, lane, a.mask_u8 + e * NACT);
+        if (has(F_MASK_BITS))
+            mask_bits(rays, lane, reinterpret_cast<uint32_t*>(ws + SM_BITS), a.mask_bits + e * SB_MASK_BITS_BYTES);
+        if (has(F_INFO)) info_scatter<T>(rec, lane, ginfo, hist_off);
+
+        if (dirty) reinterpret_cast<uint2*>(a.rec + e * REC)[lane] = reinterpret_cast<const uint2*>(rec)[lane];
+        __syncwarp();
     }
-    if (staged && lane == 0) bulk_wait_all();
 }
 
 // ---------------------------------------------------------------------------
@@ -965,7 +1003,12 @@ struct OccEntry {
 std::mutex g_mu;
 OccEntry g_occ[64];
 int g_nocc = 0;
+const void* g_attr_fn[64];
+int g_attr_dev[64];
+int g_nattr = 0;
 
+// Opt every env_kernel instantiation into the device's full per-block shared
+// memory once, then cache the occupancy of each shared-memory size.
 int blocks_per_sm(const void* fn, int dev, int smem, int* out) {
     std::lock_guard<std::mutex> lock(g_mu);
     for (int i = 0; i < g_nocc; ++i)
@@ -973,10 +1016,22 @@ int blocks_per_sm(const void* fn, int dev, int smem, int* out) {
             *out = g_occ[i].blocks;
             return SB_OK;
         }
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    bool opted = false;
+    for (int i = 0; i < g_nattr; ++i)
+        if (g_attr_fn[i] == fn && g_attr_dev[i] == dev) opted = true;
+    if (!opted) {
+        int optin = 0;
+        cudaError_t e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+        if (g_nattr < 64) {
+            g_attr_fn[g_nattr] = fn;
+            g_attr_dev[g_nattr++] = dev;
+        }
+    }
     int nb = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, sb::WARPS * 32, smem);
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, sb::WARPS * 32, smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
     if (nb < 1) return fail(SB_E_CUDA, "kernel does not fit on an SM with %d bytes of shared memory", smem);
     if (g_nocc < 64) g_occ[g_nocc++] = OccEntry{fn, dev, smem, nb};
@@ -997,33 +1052,17 @@ int sm_count(int dev, int* out) {
     return SB_OK;
 }
 
-// Shared memory plan of one warp: record, rays, two hidden-piece rows, then
-// the staging buffers that this launch needs.
-void plan_smem(sb::KArgs& k, bool info, int dtype) {
+// Shared memory plan of one warp: record, rays, two hidden-piece rows, and
+// the bit buffer of bit-packed masks.
+void plan_smem(sb::KArgs& k) {
     int off = sb::SM_FIXED;
-    k.sm_r1 = k.sm_hist = k.sm_mask = k.sm_bits = 0;
-    if (info) {
-        const int pb = dtype == SB_DTYPE_F32 ? 400 : 200;
-        k.sm_r1 = off;
-        off += ((43 * pb + 15) / 16) * 16;
-        k.sm_hist = off;
-        off += 32 * pb;
-    }
-    if (k.flags & sb::F_MASK_U8) {
-        k.sm_mask = off;
-        off += sb::NACT;
-    }
-    if (k.flags & sb::F_MASK_BITS) {
-        k.sm_bits = off;
-        off += 1264;
-    }
+    if (k.flags & sb::F_MASK_BITS) off += 1264;
     k.sm_warp = (off + 127) / 128 * 128;
 }
 
-int launch_env(sb::KArgs& k, int dtype, cudaStream_t st) {
-    if (k.n == 0) return SB_OK;
-    plan_smem(k, (k.flags & sb::F_INFO) != 0, dtype);
-    const void* fn = dtype == SB_DTYPE_F32 ? (const void*)sb::env_kernel<float> : (const void*)sb::env_kernel<uint16_t>;
+template <typename T, int MODE>
+int launch_mode(sb::KArgs& k, cudaStream_t st) {
+    const void* fn = (const void*)sb::env_kernel<T, MODE>;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -1034,13 +1073,31 @@ int launch_env(sb::KArgs& k, int dtype, cudaStream_t st) {
     int64_t blocks = (k.n + sb::WARPS - 1) / sb::WARPS;
     const int64_t cap = (int64_t)sms * nb;
     if (blocks > cap) blocks = cap;
-    if (dtype == SB_DTYPE_F32)
-        sb::env_kernel<float><<<(unsigned)blocks, sb::WARPS * 32, smem, st>>>(k);
-    else
-        sb::env_kernel<uint16_t><<<(unsigned)blocks, sb::WARPS * 32, smem, st>>>(k);
+    sb::env_kernel<T, MODE><<<(unsigned)blocks, sb::WARPS * 32, smem, st>>>(k);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "env_kernel launch");
     return SB_OK;
+}
+
+// The step kernels (apply + step + propose, one policy) are compiled apart
+// from the generic one; everything else goes through MODE_GENERIC.
+int launch_env(sb::KArgs& k, int dtype, cudaStream_t st) {
+    if (k.n == 0) return SB_OK;
+    plan_smem(k);
+    const uint32_t step = sb::F_APPLY | sb::F_STEP | sb::F_PROPOSE;
+    const uint32_t off = sb::F_RESET_PLANES | sb::F_RESET_POOL | sb::F_SAMPLE_OUT | sb::F_HAS_LEGAL;
+    int mode = sb::MODE_GENERIC;
+    if ((k.flags & step) == step && !(k.flags & off))
+        mode = k.policy == SB_POLICY_UNIFORM ? sb::MODE_STEP_UNIFORM : sb::MODE_STEP_GUMBEL;
+    const bool f32 = dtype == SB_DTYPE_F32;
+    switch (mode) {
+        case sb::MODE_STEP_UNIFORM:
+            return f32 ? launch_mode<float, sb::MODE_STEP_UNIFORM>(k, st) : launch_mode<uint16_t, sb::MODE_STEP_UNIFORM>(k, st);
+        case sb::MODE_STEP_GUMBEL:
+            return f32 ? launch_mode<float, sb::MODE_STEP_GUMBEL>(k, st) : launch_mode<uint16_t, sb::MODE_STEP_GUMBEL>(k, st);
+        default:
+            return f32 ? launch_mode<float, sb::MODE_GENERIC>(k, st) : launch_mode<uint16_t, sb::MODE_GENERIC>(k, st);
+    }
 }
 
 int check_info(const void* p, int dtype, int layout) {

@@ -13,8 +13,9 @@ one ply over all envs = one launch of the fused step kernel.  Synthetic data:
 there is no dataset; setups and actions come from Philox.
 
 Timing: W untimed warm-up steps; then K steps, each bracketed by CUDA events
-on the buffer's stream, with a 512 MiB write between timed steps to flush the
-126 MB L2 (outside the bracketed interval); barrier + synchronize on both
+on the buffer's stream, with a 512 MiB write and a 256 MiB read between timed
+steps to flush the 126 MB L2 (outside the bracketed interval); barrier +
+synchronize on both
 sides; max over ranks.  Multi-GPU (torchrun): each rank owns its own 4096 envs
 (global env indices rank*4096 ...), no collective on the step path (weak
 scaling); an NCCL all-gather of the episode statistics follows the timed
@@ -238,7 +239,11 @@ def main() -> None:
     buf.reset_all_from_pool()
     for _ in range(args.warmup):
         buf.step(None)
+    # L2 flush between timed steps: write a buffer larger than the 126 MB L2,
+    # then read another one, so the L2 holds only clean unrelated lines when
+    # the timed step starts (its write-backs do not land inside the step).
     flush = torch.empty(args.flush_mib << 20, dtype=torch.uint8, device=dev)
+    flush_rd = torch.ones((args.flush_mib << 20) // 8 // 2, dtype=torch.int64, device=dev)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     stream = torch.cuda.current_stream(dev)
@@ -247,6 +252,7 @@ def main() -> None:
     with ClockSampler(dev) as clocks:
         for k in range(args.steps):
             flush.fill_(k & 0xFF)
+            flush_rd.max()
             starts[k].record(stream)
             buf.step(None)
             ends[k].record(stream)
@@ -332,7 +338,7 @@ def main() -> None:
                             "u8 [B,100,100] mask; one step = one fused-kernel ply over all envs",
                 "envs_per_gpu": B,
                 "parallelism": f"env-sharded x{world}, no step-path collective",
-                "l2": f"flushed between timed steps ({args.flush_mib} MiB write)",
+                "l2": f"flushed between timed steps ({args.flush_mib} MiB write, then {args.flush_mib // 2} MiB read)",
             },
             "roofline": {
                 "bound": "hbm",
