@@ -57,6 +57,24 @@ class SbStepOut(ctypes.Structure):
     ]
 
 
+class SbTraj(ctypes.Structure):
+    _fields_ = [
+        ("infostate", vp),
+        ("info_dtype", ctypes.c_int32),
+        ("info_layout", ctypes.c_int32),
+        ("mask_u8", vp),
+        ("mask_bits", vp),
+        ("action", vp),
+        ("logprob", vp),
+        ("reward", vp),
+        ("done", vp),
+        ("hash", vp),
+        ("stats", vp),
+        ("n_slots", ctypes.c_int64),
+        ("slot0", ctypes.c_int64),
+    ]
+
+
 class SbPolicy(ctypes.Structure):
     _fields_ = [("kind", ctypes.c_int32), ("reserved", ctypes.c_int32), ("logits", vp)]
 
@@ -86,6 +104,9 @@ _SIGS = {
     "sb_apply_actions": (ctypes.c_int, [ctypes.POINTER(SbState), vp, vp]),
     "sb_step": (ctypes.c_int, [ctypes.POINTER(SbState), vp, ctypes.c_int64, ctypes.POINTER(SbPolicy), ctypes.c_int,
                                ctypes.POINTER(SbStepOut), vp]),
+    "sb_rollout": (ctypes.c_int, [ctypes.POINTER(SbState), ctypes.c_int64, ctypes.POINTER(SbPolicy), ctypes.c_int,
+                                  ctypes.c_int32, ctypes.POINTER(SbTraj), vp]),
+    "sb_belief_resample": (ctypes.c_int, [ctypes.POINTER(SbState), ctypes.POINTER(SbState), vp, vp]),
     "sb_sample_actions": (ctypes.c_int, [ctypes.POINTER(SbState), ctypes.c_int64, ctypes.POINTER(SbPolicy), vp, vp, vp]),
     "sb_legal_mask_u8": (ctypes.c_int, [ctypes.POINTER(SbState), vp, vp]),
     "sb_legal_mask_bits": (ctypes.c_int, [ctypes.POINTER(SbState), vp, vp]),

@@ -507,6 +507,18 @@ class StrategoRolloutBuffer:
                        acts.data_ptr(), lp.data_ptr())
         return acts, lp
 
+    def resample_from(self, roots: "StrategoRolloutBuffer", root_of: torch.Tensor) -> None:
+        """Belief resampling: env e becomes a copy of ``roots`` env ``root_of[e]`` with
+        the side-not-to-move's unrevealed identities re-dealt uniformly among the
+        deals consistent with what the side to move has seen (moved pieces are
+        never a Bomb or the Flag).  Keyed by this buffer's seed and env indices."""
+        if root_of.dtype != torch.int64 or root_of.numel() != self._n:
+            raise RuntimeError("root_of must be int64 [n_games]")
+        r = root_of.to(self.device).contiguous()
+        with torch.cuda.device(self.device):
+            C.call("sb_belief_resample", ctypes.byref(roots._st), ctypes.byref(self._st), r.data_ptr(),
+                   _stream(self.device))
+
     def export_state(self) -> dict[str, torch.Tensor]:
         """Every state field in the reference's tensor layout (cpp:24-55), plus
         ``chase_hashes`` [N,2,64], ``episode`` and ``invalid_count``."""

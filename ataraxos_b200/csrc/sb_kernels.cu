@@ -73,6 +73,14 @@ struct KArgs {
     int64_t* sampled;
     float* sampled_lp;
     int32_t sm_warp;
+    // step modes: plies per launch (0 = observe only) and the output ring.
+    // Ply p of a launch reads its transition outputs (reward, done, taken
+    // action) at slot (slot0 + p) % n_slots and writes the observation of the
+    // new state (mask, infostate, proposal, hash) at slot (slot0 + p + 1) %
+    // n_slots; every output array is laid out [n_slots, n, ...].
+    int32_t n_plies;
+    int64_t n_slots;
+    int64_t slot0;
 };
 
 constexpr int WARPS = 4;  // warps (envs in flight) per CTA
@@ -679,7 +687,8 @@ __global__ void __launch_bounds__(WARPS * 32, 8) env_kernel(const KArgs a) {
     auto has = [&](uint32_t f) -> bool {
         if (kStep) {
             if (f & (F_RESET_PLANES | F_RESET_POOL | F_SAMPLE_OUT | F_HAS_LEGAL)) return false;
-            if (f & (F_APPLY | F_STEP | F_PROPOSE)) return true;
+            if (f & F_PROPOSE) return true;
+            if (f & (F_APPLY | F_STEP)) return a.n_plies > 0;
         }
         return (a.flags & f) != 0;
     };
@@ -688,6 +697,11 @@ __global__ void __launch_bounds__(WARPS * 32, 8) env_kernel(const KArgs a) {
     uint8_t* ws = smem + (threadIdx.x >> 5) * a.sm_warp;
     uint8_t* rec = ws;
     uint16_t* rays = reinterpret_cast<uint16_t*>(ws + SM_RAYS);
+    constexpr int PB = InfoGeom<T>::PB;
+    const bool compact = a.info_layout == SB_LAYOUT_COMPACT;
+    const int64_t info_env = (int64_t)(compact ? 76 : NCH) * PB;
+    const int hist_off = (compact ? 44 : 456) * PB;
+    const int np = (kStep && a.n_plies > 1) ? a.n_plies : 1;
     const int64_t nwarps = (int64_t)gridDim.x * WARPS;
     for (int64_t e = (int64_t)blockIdx.x * WARPS + (threadIdx.x >> 5); e < a.n; e += nwarps) {
         reinterpret_cast<uint2*>(rec)[lane] = reinterpret_cast<const uint2*>(a.rec + e * REC)[lane];
@@ -702,140 +716,266 @@ __global__ void __launch_bounds__(WARPS * 32, 8) env_kernel(const KArgs a) {
             dirty = true;
         }
 
-        if (has(F_APPLY)) {
-            const bool was_term = rec[R_TERM] != 0;
-            int64_t act = -1;
-            float lp = 0.0f;
-            if (!was_term) {
-                // the mover's chase ring, fetched early (used on threatening moves)
-                const int pm = rec[R_PLAYER];
-                const int rl = rec[R_CHLEN + pm];
-                const int64_t* ringm = ring2 + pm * NRING;
-                const uint64_t ring_lo = lane < rl ? (uint64_t)ringm[lane] : 0;
-                const uint64_t ring_hi = lane + 32 < rl ? (uint64_t)ringm[lane + 32] : 0;
-                int n_legal = -1;
-                if (a.actions) act = a.actions[e];
-                if (!a.actions || has(F_STEP)) {
-                    if (fld<int32_t>(rec, R_PROPPLY) == (int32_t)a.ply && rec[R_PROPKIND] == (kPol >= 0 ? kPol : a.policy) &&
-                        !a.logits) {
-                        n_legal = fld<int16_t>(rec, R_NLEGAL);
-                        if (!a.actions) {
-                            act = fld<int16_t>(rec, R_PROP);
-                            lp = fld<float>(rec, R_PROPLP);
+        for (int p = 0; p < np; ++p) {
+            const int64_t ply = a.ply + p;
+            const int64_t s_cur = (a.slot0 + p) % a.n_slots;
+            const int64_t s_next = has(F_APPLY) ? (a.slot0 + p + 1) % a.n_slots : a.slot0 % a.n_slots;
+            const int64_t ic = s_cur * a.n + e, in = s_next * a.n + e;
+            if (has(F_APPLY)) {
+                const bool was_term = rec[R_TERM] != 0;
+                int64_t act = -1;
+                float lp = 0.0f;
+                if (!was_term) {
+                    // the mover's chase ring, fetched early (used on threatening moves)
+                    const int pm = rec[R_PLAYER];
+                    const int rl = rec[R_CHLEN + pm];
+                    const int64_t* ringm = ring2 + pm * NRING;
+                    const uint64_t ring_lo = lane < rl ? (uint64_t)ringm[lane] : 0;
+                    const uint64_t ring_hi = lane + 32 < rl ? (uint64_t)ringm[lane + 32] : 0;
+                    int n_legal = -1;
+                    if (a.actions) act = a.actions[e];
+                    if (!a.actions || has(F_STEP)) {
+                        if (fld<int32_t>(rec, R_PROPPLY) == (int32_t)ply &&
+                            rec[R_PROPKIND] == (kPol >= 0 ? kPol : a.policy) && !a.logits) {
+                            n_legal = fld<int16_t>(rec, R_NLEGAL);
+                            if (!a.actions) {
+                                act = fld<int16_t>(rec, R_PROP);
+                                lp = fld<float>(rec, R_PROPLP);
+                            }
+                        } else {
+                            enumerate(rec, pm, rays, lane, cnt);
+                            n_legal = count_of(cnt);
+                            if (!a.actions) {
+                                int ac;
+                                choose<kPol>(a, rays, cnt, n_legal, e, ply, lane, ac, lp);
+                                act = ac;
+                            }
                         }
+                    }
+                    if (has(F_STEP) && n_legal == 0) {
+                        // a start position whose side to move cannot move: it
+                        // loses (the rule of stratego/env/rules.py:406-413)
+                        if (lane == 0) {
+                            fld<int8_t>(rec, R_OUTCOME) = (int8_t)(pm == 0 ? 1 : 0);
+                            rec[R_TERM] = 1;
+                            fld<int32_t>(rec, R_PROPPLY) = -1;
+                        }
+                        act = -1;
+                        __syncwarp();
                     } else {
-                        enumerate(rec, pm, rays, lane, cnt);
-                        n_legal = count_of(cnt);
-                        if (!a.actions) {
-                            int ac;
-                            choose<kPol>(a, rays, cnt, n_legal, e, a.ply, lane, ac, lp);
-                            act = ac;
+                        bool chk, flag;
+                        const bool ok = apply_env(rec, ring2, a, act, lane, ring_lo, ring_hi, chk, flag);
+                        if (ok) rays_ok = false;  // the board changed
+                        if (!ok) {
+                            if (lane == 0) fld<int32_t>(rec, R_INVALID) += 1;
+                            __syncwarp();
+                        } else if (chk) {
+                            enumerate(rec, rec[R_PLAYER], rays, lane, cnt);
+                            rays_ok = true;
+                            if (count_of(cnt) == 0) {
+                                if (lane == 0) {
+                                    fld<int8_t>(rec, R_OUTCOME) = (int8_t)(rec[R_PLAYER] == 0 ? 1 : 0);
+                                    rec[R_TERM] = 1;
+                                }
+                                __syncwarp();
+                            }
                         }
                     }
                 }
-                if (has(F_STEP) && n_legal == 0) {
-                    // a start position whose side to move cannot move: it
-                    // loses (the rule of stratego/env/rules.py:406-413)
-                    if (lane == 0) {
-                        fld<int8_t>(rec, R_OUTCOME) = (int8_t)(pm == 0 ? 1 : 0);
-                        rec[R_TERM] = 1;
-                        fld<int32_t>(rec, R_PROPPLY) = -1;
+                const bool term = rec[R_TERM] != 0;
+                if (lane == 0) {
+                    if (term) fld<int32_t>(rec, R_TSINCE) += 1;
+                    const int8_t oc = fld<int8_t>(rec, R_OUTCOME);
+                    if (a.reward) a.reward[ic] = oc == 0 ? 1.0f : (oc == 1 ? -1.0f : 0.0f);
+                    if (a.done) a.done[ic] = term ? 1 : 0;
+                    if (a.action_taken) a.action_taken[ic] = act;
+                    if (a.logprob_taken) a.logprob_taken[ic] = lp;
+                    if (a.stats && term && !was_term) {
+                        atomicAdd(reinterpret_cast<unsigned long long*>(&a.stats[0]), 1ull);
+                        atomicAdd(reinterpret_cast<unsigned long long*>(&a.stats[oc == 0 ? 1 : (oc == 1 ? 2 : 3)]), 1ull);
+                        atomicAdd(reinterpret_cast<unsigned long long*>(&a.stats[4]),
+                                  (unsigned long long)fld<int32_t>(rec, R_MOVENUM));
                     }
-                    act = -1;
-                    __syncwarp();
-                } else {
-                    bool chk, flag;
-                    const bool ok = apply_env(rec, ring2, a, act, lane, ring_lo, ring_hi, chk, flag);
-                    if (!ok) {
-                        if (lane == 0) fld<int32_t>(rec, R_INVALID) += 1;
-                        __syncwarp();
-                    } else if (chk) {
-                        enumerate(rec, rec[R_PLAYER], rays, lane, cnt);
-                        rays_ok = true;
-                        if (count_of(cnt) == 0) {
-                            if (lane == 0) {
-                                fld<int8_t>(rec, R_OUTCOME) = (int8_t)(rec[R_PLAYER] == 0 ? 1 : 0);
-                                rec[R_TERM] = 1;
-                            }
-                            __syncwarp();
-                        }
-                    }
+                }
+                __syncwarp();
+                dirty = true;
+                if (has(F_AUTO_RESET) && term) {
+                    reset_env(rec, ring2, a, e, true, lane);
+                    rays_ok = false;
                 }
             }
-            const bool term = rec[R_TERM] != 0;
-            if (lane == 0) {
-                if (term) fld<int32_t>(rec, R_TSINCE) += 1;
-                const int8_t oc = fld<int8_t>(rec, R_OUTCOME);
-                if (a.reward) a.reward[e] = oc == 0 ? 1.0f : (oc == 1 ? -1.0f : 0.0f);
-                if (a.done) a.done[e] = term ? 1 : 0;
-                if (a.action_taken) a.action_taken[e] = act;
-                if (a.logprob_taken) a.logprob_taken[e] = lp;
-                if (a.stats && term && !was_term) {
-                    atomicAdd(reinterpret_cast<unsigned long long*>(&a.stats[0]), 1ull);
-                    atomicAdd(reinterpret_cast<unsigned long long*>(&a.stats[oc == 0 ? 1 : (oc == 1 ? 2 : 3)]), 1ull);
-                    atomicAdd(reinterpret_cast<unsigned long long*>(&a.stats[4]),
-                              (unsigned long long)fld<int32_t>(rec, R_MOVENUM));
+
+            const bool observe = has(F_MASK_U8) || has(F_MASK_BITS) || has(F_PROPOSE) || has(F_HAS_LEGAL) ||
+                                 has(F_SAMPLE_OUT);
+            int n = 0;
+            if (observe) {
+                if (!rays_ok) enumerate(rec, rec[R_PLAYER], rays, lane, cnt);
+                n = count_of(cnt);
+            }
+            // background rows of the outputs, then (after one __syncwarp) the one-hots
+            uint8_t* ginfo = nullptr;
+            if (has(F_INFO)) {
+                ginfo = reinterpret_cast<uint8_t*>(a.info) + in * info_env;
+                info_background<T>(rec, a, lane, ginfo, hist_off, a.info_layout == SB_LAYOUT_DENSE_ALL,
+                                   reinterpret_cast<T*>(ws + SM_PAT_OPP), reinterpret_cast<T*>(ws + SM_PAT_OWN));
+            }
+            if (has(F_MASK_U8)) mask_background(a.mask_u8 + in * NACT, lane);
+            if (has(F_PROPOSE) || has(F_SAMPLE_OUT)) {
+                const int64_t pp = has(F_PROPOSE) ? (has(F_APPLY) ? ply + 1 : ply) : a.ply;
+                int ac;
+                float lp;
+                choose<kPol>(a, rays, cnt, n, e, pp, lane, ac, lp);
+                if (lane == 0) {
+                    if (has(F_PROPOSE)) {
+                        fld<int16_t>(rec, R_PROP) = (int16_t)ac;
+                        fld<int32_t>(rec, R_PROPPLY) = a.logits ? -1 : (int32_t)pp;
+                        rec[R_PROPKIND] = (uint8_t)(kPol >= 0 ? kPol : a.policy);
+                        fld<int16_t>(rec, R_NLEGAL) = (int16_t)n;
+                        fld<float>(rec, R_PROPLP) = lp;
+                        if (a.next_action) a.next_action[in] = (int16_t)ac;
+                        if (a.next_logprob) a.next_logprob[in] = lp;
+                    }
+                    if (has(F_SAMPLE_OUT)) {
+                        if (a.sampled) a.sampled[e] = ac;
+                        if (a.sampled_lp) a.sampled_lp[e] = lp;
+                    }
                 }
+                if (has(F_PROPOSE)) dirty = true;
+            }
+            if (lane == 0) {
+                if (has(F_HAS_LEGAL)) a.has_legal[e] = n > 0;
+                if (has(F_HASH)) a.hash[in] = fld<int64_t>(rec, R_ZHASH);
             }
             __syncwarp();
-            dirty = true;
-            if (has(F_AUTO_RESET) && term) {
-                reset_env(rec, ring2, a, e, true, lane);
-                rays_ok = false;
-            }
+            if (has(F_MASK_U8)) mask_scatter(rays, lane, a.mask_u8 + in * NACT);
+            if (has(F_MASK_BITS))
+                mask_bits(rays, lane, reinterpret_cast<uint32_t*>(ws + SM_BITS), a.mask_bits + in * SB_MASK_BITS_BYTES);
+            if (has(F_INFO)) info_scatter<T>(rec, lane, ginfo, hist_off);
+            __syncwarp();
         }
-
-        const bool observe = has(F_MASK_U8) || has(F_MASK_BITS) || has(F_PROPOSE) || has(F_HAS_LEGAL) || has(F_SAMPLE_OUT);
-        int n = 0;
-        if (observe) {
-            if (!rays_ok) enumerate(rec, rec[R_PLAYER], rays, lane, cnt);
-            n = count_of(cnt);
-        }
-        // background rows of the outputs, then (after one __syncwarp) the one-hots
-        uint8_t* ginfo = nullptr;
-        int hist_off = 0;
-        if (has(F_INFO)) {
-            constexpr int PB = InfoGeom<T>::PB;
-            const bool compact = a.info_layout == SB_LAYOUT_COMPACT;
-            ginfo = reinterpret_cast<uint8_t*>(a.info) + e * (int64_t)(compact ? 76 : NCH) * PB;
-            hist_off = (compact ? 44 : 456) * PB;
-            info_background<T>(rec, a, lane, ginfo, hist_off, a.info_layout == SB_LAYOUT_DENSE_ALL,
-                               reinterpret_cast<T*>(ws + SM_PAT_OPP), reinterpret_cast<T*>(ws + SM_PAT_OWN));
-        }
-        if (has(F_MASK_U8)) mask_background(a.mask_u8 + e * NACT, lane);
-        if (has(F_PROPOSE) || has(F_SAMPLE_OUT)) {
-            const int64_t pp = has(F_PROPOSE) ? a.propose_ply : a.ply;
-            int ac;
-            float lp;
-            choose<kPol>(a, rays, cnt, n, e, pp, lane, ac, lp);
-            if (lane == 0) {
-                if (has(F_PROPOSE)) {
-                    fld<int16_t>(rec, R_PROP) = (int16_t)ac;
-                    fld<int32_t>(rec, R_PROPPLY) = a.logits ? -1 : (int32_t)pp;
-                    rec[R_PROPKIND] = (uint8_t)(kPol >= 0 ? kPol : a.policy);
-                    fld<int16_t>(rec, R_NLEGAL) = (int16_t)n;
-                    fld<float>(rec, R_PROPLP) = lp;
-                    if (a.next_action) a.next_action[e] = (int16_t)ac;
-                    if (a.next_logprob) a.next_logprob[e] = lp;
-                }
-                if (has(F_SAMPLE_OUT)) {
-                    if (a.sampled) a.sampled[e] = ac;
-                    if (a.sampled_lp) a.sampled_lp[e] = lp;
-                }
-            }
-            if (has(F_PROPOSE)) dirty = true;
-        }
-        if (lane == 0) {
-            if (has(F_HAS_LEGAL)) a.has_legal[e] = n > 0;
-            if (has(F_HASH)) a.hash[e] = fld<int64_t>(rec, R_ZHASH);
-        }
-        __syncwarp();
-        if (has(F_MASK_U8)) mask_scatter(rays, lane, a.mask_u8 + e * NACT);
-        if (has(F_MASK_BITS))
-            mask_bits(rays, lane, reinterpret_cast<uint32_t*>(ws + SM_BITS), a.mask_bits + e * SB_MASK_BITS_BYTES);
-        if (has(F_INFO)) info_scatter<T>(rec, lane, ginfo, hist_off);
 
         if (dirty) reinterpret_cast<uint2*>(a.rec + e * REC)[lane] = reinterpret_cast<const uint2*>(rec)[lane];
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Belief resampling for search (north-star; no reference kernel)
+// ---------------------------------------------------------------------------
+//
+// Sample env e starts as a copy of root r = root_of[e] whose opponent (the
+// side not to move) has its unrevealed pieces' identities re-dealt: the
+// moved unrevealed squares first draw, without replacement, from the movable
+// identities of that multiset (a moved piece is never a Bomb or the Flag),
+// then the remaining identities are shuffled over the unmoved unrevealed
+// squares.  Both draws are uniform, so the deal is uniform over the
+// assignments consistent with what the side to move has seen.  Philox key:
+// the samples' seed; counter: (global sample index, block, TAG_BELIEF).
+// The copy keeps the board's flags, counters, history and two-square state;
+// its chase rings start empty (their hashes described the true identities)
+// and its Zobrist hash is recomputed.
+__global__ void __launch_bounds__(WARPS * 32) belief_kernel(const uint8_t* root_rec, int64_t n_roots,
+                                                           const int64_t* root_of, KArgs a) {
+    __shared__ __align__(16) uint8_t srec[WARPS][REC];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    uint8_t* rec = srec[w];
+    const int64_t nwarps = (int64_t)gridDim.x * WARPS;
+    for (int64_t e = (int64_t)blockIdx.x * WARPS + w; e < a.n; e += nwarps) {
+        int64_t r = root_of[e];
+        const bool bad = r < 0 || r >= n_roots;
+        if (bad) r = 0;
+        reinterpret_cast<uint2*>(rec)[lane] = reinterpret_cast<const uint2*>(root_rec + r * REC)[lane];
+        __syncwarp();
+        const int opp = 1 - rec[R_PLAYER];
+        unsigned hid[4], mov[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int sq = lane + 32 * k;
+            const uint8_t c = sq < NSQ ? rec[sq] : 0;
+            const bool h = (c & C_OCC) && ((c >> 4) & 1) == opp && !(c & C_REV);
+            hid[k] = __ballot_sync(FULL, h);
+            mov[k] = __ballot_sync(FULL, h && (c & C_MOVED));
+        }
+        if (lane == 0) {
+            if (bad && a.status) atomicOr(a.status, SB_STATUS_BAD_SETUP);
+            uint8_t msq[40], usq[40], pcs[40];
+            int nm = 0, nu = 0, nmov = 0, nimm = 0;
+            uint8_t movp[40], immp[40];
+            for (int k = 0; k < 4; ++k) {
+                unsigned hb = hid[k];
+                while (hb) {
+                    const int b = __ffs(hb) - 1;
+                    hb &= hb - 1;
+                    const int sq = 32 * k + b;
+                    const int pc = rec[sq] & C_PIECE;
+                    if (nm + nu < 40) {
+                        if ((mov[k] >> b) & 1) msq[nm++] = (uint8_t)sq;
+                        else usq[nu++] = (uint8_t)sq;
+                        if (can_move(pc)) movp[nmov++] = (uint8_t)pc;
+                        else immp[nimm++] = (uint8_t)pc;
+                    }
+                }
+            }
+            // identities: movable ones first, then bombs / flag
+            int np_ = 0;
+            for (int i = 0; i < nmov; ++i) pcs[np_++] = movp[i];
+            for (int i = 0; i < nimm; ++i) pcs[np_++] = immp[i];
+            const int64_t ge = a.env_base + e;
+            uint32_t words[4];
+            int used = 4, blk = 0;
+            auto draw = [&](uint32_t bound) -> int {
+                if (used == 4) {
+                    const uint4 q = philox((uint32_t)ge, (uint32_t)blk++, (uint32_t)((uint64_t)ge >> 32), TAG_BELIEF,
+                                           a.seed);
+                    words[0] = q.x;
+                    words[1] = q.y;
+                    words[2] = q.z;
+                    words[3] = q.w;
+                    used = 0;
+                }
+                return (int)mulshift(words[used++], bound);
+            };
+            // 1) moved squares draw from the movable identities (partial Fisher-Yates)
+            const int take = nm < nmov ? nm : nmov;
+            for (int i = 0; i < take; ++i) {
+                const int j = i + draw((uint32_t)(nmov - i));
+                const uint8_t t = pcs[i];
+                pcs[i] = pcs[j];
+                pcs[j] = t;
+            }
+            // 2) the rest shuffled over the unmoved squares (Fisher-Yates on the tail)
+            for (int i = np_ - 1; i > take; --i) {
+                const int j = take + draw((uint32_t)(i - take + 1));
+                const uint8_t t = pcs[i];
+                pcs[i] = pcs[j];
+                pcs[j] = t;
+            }
+            for (int i = 0; i < nm; ++i) rec[msq[i]] = (uint8_t)((rec[msq[i]] & ~C_PIECE) | pcs[i]);
+            for (int i = 0; i < nu; ++i) rec[usq[i]] = (uint8_t)((rec[usq[i]] & ~C_PIECE) | pcs[nm + i]);
+            rec[R_CHHEAD] = rec[R_CHHEAD + 1] = 0;
+            rec[R_CHLEN] = rec[R_CHLEN + 1] = 0;
+            fld<int8_t>(rec, R_CHLAST) = -1;
+            fld<int8_t>(rec, R_CHLAST + 1) = -1;
+            fld<int32_t>(rec, R_PROPPLY) = -1;
+            fld<int16_t>(rec, R_PROP) = -1;
+        }
+        __syncwarp();
+        uint64_t h = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int sq = lane + 32 * k;
+            if (sq < NSQ) {
+                const uint8_t c = rec[sq];
+                if (c & C_OCC) h ^= zob(a.zob, sq, (c >> 4) & 1, c & C_PIECE);
+            }
+        }
+        h = warp_xor64(h);
+        if (lane == 0) fld<uint64_t>(rec, R_ZHASH) = h;
+        int4* rg = reinterpret_cast<int4*>(a.ring + e * 2 * NRING);
+        rg[lane] = make_int4(0, 0, 0, 0);
+        rg[lane + 32] = make_int4(0, 0, 0, 0);
+        __syncwarp();
+        reinterpret_cast<uint2*>(a.rec + e * REC)[lane] = reinterpret_cast<const uint2*>(rec)[lane];
         __syncwarp();
     }
 }
@@ -991,6 +1131,9 @@ sb::KArgs base_args(const sb_state* s) {
     k.ts_limit = s->two_square_limit;
     k.status = s->status;
     k.policy = SB_POLICY_UNIFORM;
+    k.n_plies = 1;
+    k.n_slots = 1;
+    k.slot0 = 0;
     return k;
 }
 
@@ -1225,6 +1368,73 @@ int sb_step(const sb_state* s, const int64_t* actions, int64_t ply, const sb_pol
     k.next_logprob = o.next_logprob;
     k.stats = o.stats;
     return launch_env(k, dtype, (cudaStream_t)stream);
+}
+
+int sb_rollout(const sb_state* s, int64_t ply, const sb_policy* policy, int auto_reset, int32_t n_plies,
+               const sb_traj* traj, void* stream) {
+    int rc = check_state(s);
+    if (rc != SB_OK || s->n == 0) return rc;
+    if ((rc = check_policy(policy)) != SB_OK) return rc;
+    if (!traj) return fail(SB_E_ARG, "traj is NULL");
+    if (n_plies < 0) return fail(SB_E_ARG, "n_plies < 0");
+    if (traj->n_slots < 1 || traj->slot0 < 0) return fail(SB_E_ARG, "bad trajectory ring (n_slots < 1 or slot0 < 0)");
+    if (policy && policy->logits && n_plies > 1) return fail(SB_E_ARG, "logits in memory cover one ply only");
+    if (auto_reset && n_plies > 0 && !s->setup_pool) return fail(SB_E_NOPOOL, "auto_reset needs a setup pool");
+    sb::KArgs k = base_args(s);
+    k.flags = sb::F_APPLY | sb::F_STEP | sb::F_PROPOSE | (auto_reset ? sb::F_AUTO_RESET : 0);
+    k.ply = ply;
+    k.n_plies = n_plies;
+    k.n_slots = traj->n_slots;
+    k.slot0 = traj->slot0;
+    if (policy) {
+        k.policy = policy->kind;
+        k.logits = policy->logits;
+    }
+    int dtype = SB_DTYPE_F32;
+    if (traj->infostate) {
+        if ((rc = check_info(traj->infostate, traj->info_dtype, traj->info_layout)) != SB_OK) return rc;
+        k.flags |= sb::F_INFO;
+        k.info = traj->infostate;
+        k.info_layout = traj->info_layout;
+        dtype = traj->info_dtype;
+    }
+    if (traj->mask_u8) {
+        if (!aligned(traj->mask_u8, 16)) return fail(SB_E_ARG, "mask_u8 not 16-byte aligned");
+        k.flags |= sb::F_MASK_U8;
+        k.mask_u8 = traj->mask_u8;
+    }
+    if (traj->mask_bits) {
+        if (!aligned(traj->mask_bits, 2)) return fail(SB_E_ARG, "mask_bits not 2-byte aligned");
+        k.flags |= sb::F_MASK_BITS;
+        k.mask_bits = traj->mask_bits;
+    }
+    if (traj->hash) k.flags |= sb::F_HASH;
+    k.hash = traj->hash;
+    k.next_action = traj->action;
+    k.next_logprob = traj->logprob;
+    k.reward = traj->reward;
+    k.done = traj->done;
+    k.stats = traj->stats;
+    return launch_env(k, dtype, (cudaStream_t)stream);
+}
+
+int sb_belief_resample(const sb_state* roots, const sb_state* samples, const int64_t* root_of, void* stream) {
+    int rc = check_state(roots);
+    if (rc != SB_OK) return rc;
+    if ((rc = check_state(samples)) != SB_OK) return rc;
+    if (samples->n == 0) return SB_OK;
+    if (roots->n < 1) return fail(SB_E_ARG, "no roots");
+    if (!root_of) return fail(SB_E_ARG, "root_of is NULL");
+    sb::KArgs k = base_args(samples);
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if ((rc = sm_count(dev, &sms)) != SB_OK) return rc;
+    int64_t blocks = (samples->n + sb::WARPS - 1) / sb::WARPS;
+    if (blocks > (int64_t)sms * 16) blocks = (int64_t)sms * 16;
+    sb::belief_kernel<<<(unsigned)blocks, sb::WARPS * 32, 0, (cudaStream_t)stream>>>(roots->records, roots->n, root_of, k);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? SB_OK : cuda_fail(e, "belief_kernel launch");
 }
 
 int sb_sample_actions(const sb_state* s, int64_t ply, const sb_policy* policy, int64_t* actions, float* logprob,

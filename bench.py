@@ -197,175 +197,329 @@ def run_reference(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
-def main() -> None:
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=3000)
-    ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--envs", type=int, default=4096, help="envs per GPU")
-    ap.add_argument("--e2e-steps", type=int, default=500)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--flush-mib", type=int, default=512)
-    args = ap.parse_args()
-    if args.warmup < 3:
-        raise SystemExit("--warmup must be >= 3")
+def _profile_traffic(name: str) -> float | None:
+    """dram_bytes_per_launch recorded from the ncu capture summarised in profiles/<name>."""
+    f = ROOT / "profiles" / name
+    try:
+        for line in f.read_text().splitlines():
+            if line.startswith("dram_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except Exception:
+        return None
+    return None
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference":
-        run_reference(args, rank)
-        return
 
-    import torch.distributed as dist
+class Ctx:
+    def __init__(self, args):
+        import torch.distributed as dist
 
-    from ataraxos_b200 import StrategoRolloutBuffer
+        self.args = args
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        self.dist = dist
+        if self.world > 1:
+            from datetime import timedelta
 
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=self.dev)
+        self.stream = torch.cuda.current_stream(self.dev)
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
+    def max_over_ranks(self, v: float) -> float:
+        t = torch.tensor([v], dtype=torch.float64, device=self.dev)
+        if self.world > 1:
+            self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
 
-    B = args.envs
-    buf = StrategoRolloutBuffer(B, local, seed=SEED, env_base=rank * B, pool_size=POOL, pool_seed=SEED,
-                                obs_dtype=torch.bfloat16, obs_layout="dense", mask_format="u8")
-    buf.reset_all_from_pool()
-    for _ in range(args.warmup):
-        buf.step(None)
-    # L2 flush between timed steps: write a buffer larger than the 126 MB L2,
-    # then read another one, so the L2 holds only clean unrelated lines when
-    # the timed step starts (its write-backs do not land inside the step).
-    flush = torch.empty(args.flush_mib << 20, dtype=torch.uint8, device=dev)
-    flush_rd = torch.ones((args.flush_mib << 20) // 8 // 2, dtype=torch.int64, device=dev)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    stream = torch.cuda.current_stream(dev)
-    barrier()
-    torch.cuda.synchronize(dev)
-    with ClockSampler(dev) as clocks:
-        for k in range(args.steps):
-            flush.fill_(k & 0xFF)
-            flush_rd.max()
-            starts[k].record(stream)
-            buf.step(None)
-            ends[k].record(stream)
-        torch.cuda.synchronize(dev)
-        barrier()
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = sum(step_ms)
-    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms = float(t.item())
-    value = world * B * args.steps / (total_ms / 1e3)
-    launch_ms = total_ms / args.steps
+    def gather_stats(self, stats: torch.Tensor) -> list[int]:
+        """End-of-rollout NCCL all-gather of each rank's int64[5] episode statistics."""
+        if self.world > 1:
+            g = torch.empty((self.world, 5), dtype=torch.int64, device=self.dev)
+            self.dist.all_gather_into_tensor(g, stats.contiguous())
+            return g.sum(0).tolist()
+        return stats.tolist()
 
-    # end-of-rollout statistics: NCCL all-gather of int64[5] per rank (off the step path)
-    stats = buf.episode_stats().clone()
-    if world > 1:
-        gathered = torch.empty((world, 5), dtype=torch.int64, device=dev)
-        dist.all_gather_into_tensor(gathered, stats)
-        stats_all = gathered.sum(0).tolist()
-    else:
-        stats_all = stats.tolist()
 
-    # e2e through the public API with host buffers: each step copies the
-    # actions (int64[B]) from pinned host memory to the device, runs the fused
-    # step, and reads reward, done and the next proposed actions back into
-    # pinned host memory (the host picks the next actions from them).
+def timed_launches(ctx: Ctx, launch, k: int, flush_mib: int):
+    """k launches, each bracketed by CUDA events; L2 flushed between them when flush_mib > 0."""
+    flush = flush_rd = None
+    if flush_mib > 0:
+        flush = torch.empty(flush_mib << 20, dtype=torch.uint8, device=ctx.dev)
+        flush_rd = torch.ones((flush_mib << 20) // 16, dtype=torch.int64, device=ctx.dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(k)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(k)]
+    ctx.barrier()
+    torch.cuda.synchronize(ctx.dev)
+    with ClockSampler(ctx.dev) as clocks:
+        for i in range(k):
+            if flush is not None:
+                # write a buffer larger than the 126 MB L2, then read another, so
+                # the L2 holds only clean unrelated lines when the launch starts
+                flush.fill_(i & 0xFF)
+                flush_rd.max()
+            starts[i].record(ctx.stream)
+            launch(i)
+            ends[i].record(ctx.stream)
+        torch.cuda.synchronize(ctx.dev)
+        ctx.barrier()
+    total_ms = ctx.max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(starts, ends)))
+    return total_ms, clocks.summary()
+
+
+def e2e_loop(ctx: Ctx, buf, steps: int, policy: str = "uniform") -> tuple[float, int, int]:
+    """The public API with host buffers: per step the actions (int64[B]) go
+    host->device from pinned memory, the fused step runs, and reward, done and
+    the next proposed actions come back into pinned memory (the host takes
+    the proposals as its next actions).  Returns (updates/s, h2d, d2h bytes)."""
+    B = buf.n_games
     h_act = torch.empty(B, dtype=torch.int64, pin_memory=True)
     h_rew = torch.empty(B, dtype=torch.float32, pin_memory=True)
     h_done = torch.empty(B, dtype=torch.uint8, pin_memory=True)
     h_next = torch.empty(B, dtype=torch.int16, pin_memory=True)
-    out = buf.step(None)
+    out = buf.step(None, policy=policy)
     h_next.copy_(out.next_action)
-    e2e_steps = args.e2e_steps
-    barrier()
-    torch.cuda.synchronize(dev)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        h_act.copy_(h_next)  # host-side policy: take the proposals
-        out = buf.step(h_act)
+    ctx.barrier()
+    torch.cuda.synchronize(ctx.dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ctx.stream)
+    for _ in range(steps):
+        h_act.copy_(h_next)
+        out = buf.step(h_act, policy=policy)
         h_rew.copy_(out.reward, non_blocking=True)
         h_done.copy_(out.done.view(torch.uint8), non_blocking=True)
         h_next.copy_(out.next_action, non_blocking=True)
-        stream.synchronize()
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    e2e_ms = e0.elapsed_time(e1)
-    t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_ms = float(t.item())
-    e2e = world * B * e2e_steps / (e2e_ms / 1e3)
+        ctx.stream.synchronize()
+    e1.record(ctx.stream)
+    torch.cuda.synchronize(ctx.dev)
+    ctx.barrier()
+    ms = ctx.max_over_ranks(e0.elapsed_time(e1))
+    return ctx.world * B * steps / (ms / 1e3), B * 8, B * (4 + 1 + 2)
 
-    if rank == 0:
+
+def run_step_config(ctx: Ctx, cfg: int) -> dict:
+    """Configs 2 (4096 envs/GPU, uniform) and 3 (262144 envs split over the GPUs, Gumbel-max
+    over virtual N(0,1) logits, 1M-entry pool): one fused-kernel ply per step."""
+    from ataraxos_b200 import StrategoRolloutBuffer
+
+    a = ctx.args
+    if cfg == 2:
+        B, pool, policy, env_base = a.envs, POOL, "uniform", ctx.rank * a.envs
+    else:
+        total = a.envs if a.envs != 4096 else 262144
+        B, pool, policy = total // ctx.world, 1 << 20, "gumbel"
+        env_base = ctx.rank * B
+    buf = StrategoRolloutBuffer(B, ctx.local, seed=SEED, env_base=env_base, pool_size=pool, pool_seed=SEED,
+                                obs_dtype=torch.bfloat16, obs_layout="dense", mask_format="u8")
+    buf.reset_all_from_pool()
+    for _ in range(a.warmup):
+        buf.step(None, policy=policy)
+    flush = a.flush_mib if cfg == 2 else 0  # config 3 writes 6.7 GB/GPU per step: far above L2
+    total_ms, clocks = timed_launches(ctx, lambda i: buf.step(None, policy=policy), a.steps, flush)
+    launch_ms = total_ms / a.steps
+    stats = ctx.gather_stats(buf.episode_stats().clone())
+    if cfg == 2:
+        e2e, h2d, d2h = e2e_loop(ctx, buf, a.e2e_steps)
+        workload = (f"config2: {B} envs/GPU, seeded random setups (pool {pool}), uniform random legal actions, "
+                    "auto-reset, bf16 [B,488,10,10] infostate (75 live planes rewritten per ply), u8 [B,100,100] "
+                    "mask; one step = one fused-kernel ply over all envs")
+        l2 = f"flushed between timed steps ({a.flush_mib} MiB write, then {a.flush_mib // 2} MiB read)"
+        scaling = "weak"
+    else:
+        e2e, h2d, d2h = e2e_loop(ctx, buf, max(10, a.e2e_steps // 10), policy)
+        workload = (f"config3: {B * ctx.world} envs split over {ctx.world} GPU(s) ({B}/GPU), actions by Gumbel-max "
+                    "over virtual Philox N(0,1) logits of the legal moves (logits never materialised), setups from "
+                    f"a {pool}-entry pool, auto-reset, bf16 dense infostate + u8 mask")
+        l2 = "outputs of one step (25.5 KB/env) exceed L2 many times; no flush"
+        scaling = "strong"
+    return {
+        "value": ctx.world * B * a.steps / (total_ms / 1e3), "ms_per_step": launch_ms, "launch_ms": launch_ms,
+        "envs_per_launch": B, "plies_per_launch": 1, "bytes_per_update": BYTES_PER_UPDATE, "clocks": clocks,
+        "stats": stats, "e2e": {"value": e2e, "unit": "updates/s", "h2d_bytes_per_step": h2d,
+                                "d2h_bytes_per_step": d2h},
+        "gpu_launches": a.steps, "config": {"workload": workload, "envs_per_gpu": B, "l2": l2,
+                                            "parallelism": f"env-sharded x{ctx.world}, no step-path collective"},
+        "scaling": scaling, "traffic": _profile_traffic("step_kernel_config2.txt") if cfg == 2 else None,
+    }
+
+
+def run_traj_config(ctx: Ctx) -> dict:
+    """Config 4: 32768 envs/GPU, T=128 ring of compact bf16 infostate, bit-packed masks,
+    int16 actions, f32 log-probs (Gumbel over virtual N(0,1) logits), f32 rewards, u8 dones.
+    One timed launch = `plies_per_launch` plies with every record kept on chip."""
+    from ataraxos_b200 import StrategoRolloutBuffer
+    from ataraxos_b200.trajectory import TrajectoryBuffer
+
+    a = ctx.args
+    B = a.envs if a.envs != 4096 else 32768
+    T, R = 128, a.plies_per_launch
+    buf = StrategoRolloutBuffer(B, ctx.local, seed=SEED, env_base=ctx.rank * B, pool_size=POOL, pool_seed=SEED)
+    buf.reset_all_from_pool()
+    tr = TrajectoryBuffer(buf, T, policy="gumbel")
+    tr.prime()
+    for _ in range(a.warmup):
+        tr.rollout(R)
+    total_ms, clocks = timed_launches(ctx, lambda i: tr.rollout(R), a.steps, 0)
+    stats = ctx.gather_stats(tr.stats.clone())
+    # e2e: each launch is followed by a device->host read of the last ply's rewards and dones
+    h_rew = torch.empty(B, dtype=torch.float32, pin_memory=True)
+    h_done = torch.empty(B, dtype=torch.uint8, pin_memory=True)
+    steps = max(5, a.steps // 4)
+    ctx.barrier()
+    torch.cuda.synchronize(ctx.dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ctx.stream)
+    for _ in range(steps):
+        tr.rollout(R)
+        last = (tr.slot - 1) % T
+        h_rew.copy_(tr.reward[last], non_blocking=True)
+        h_done.copy_(tr.done[last], non_blocking=True)
+        ctx.stream.synchronize()
+    e1.record(ctx.stream)
+    torch.cuda.synchronize(ctx.dev)
+    e2e_ms = ctx.max_over_ranks(e0.elapsed_time(e1))
+    bpu = 15_000 + 1_250 + 2 + 4 + 4 + 1 + 512 / R
+    return {
+        "value": ctx.world * B * R * a.steps / (total_ms / 1e3), "ms_per_step": total_ms / a.steps,
+        "launch_ms": total_ms / a.steps, "envs_per_launch": B, "plies_per_launch": R, "bytes_per_update": bpu,
+        "clocks": clocks, "stats": stats,
+        "e2e": {"value": ctx.world * B * R * steps / (e2e_ms / 1e3), "unit": "updates/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": B * 5},
+        "gpu_launches": a.steps,
+        "config": {"workload": f"config4: {B} envs/GPU, T={T} ring (compact bf16 [76,10,10] infostate, bit-packed "
+                               f"mask, i16 action, f32 log-prob from virtual N(0,1) logits, f32 reward, u8 done); "
+                               f"{R} plies per launch", "envs_per_gpu": B,
+                   "l2": f"ring of {T} slots ({T * B * 16.5 / 1e9:.0f} GB) far above L2; no flush",
+                   "parallelism": f"env-sharded x{ctx.world}, no step-path collective"},
+        "scaling": "weak", "traffic": None,
+    }
+
+
+def run_search_config(ctx: Ctx) -> dict:
+    """Config 5: 64 roots/GPU advanced 150 random plies, 1000 belief samples each
+    (64,000 envs), 40-ply rollouts in one launch; bit-packed legal masks per ply
+    and terminal values per rollout."""
+    from ataraxos_b200 import StrategoRolloutBuffer
+    from ataraxos_b200.trajectory import BeliefRollouts
+
+    a = ctx.args
+    n_roots, k, depth = 64, 1000, 40
+    roots = StrategoRolloutBuffer(n_roots, ctx.local, seed=SEED, env_base=ctx.rank * n_roots, pool_size=POOL,
+                                  pool_seed=SEED)
+    roots.reset_all_from_pool()
+    for _ in range(150):
+        roots.step(None)
+    br = BeliefRollouts(roots, k, depth, seed=SEED + 1 + ctx.rank, policy="uniform")
+    br.samples.env_base = ctx.rank * n_roots * k
+    br.samples._st = br.samples._make_state()
+    for _ in range(a.warmup):
+        br.run()
+
+    def one(i):
+        br.run()
+
+    total_ms, clocks = timed_launches(ctx, one, a.steps, 0)
+    n = n_roots * k
+    h_val = torch.empty(n, dtype=torch.float32, pin_memory=True)
+    steps = max(3, a.steps // 4)
+    ctx.barrier()
+    torch.cuda.synchronize(ctx.dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ctx.stream)
+    for _ in range(steps):
+        out = br.run()
+        h_val.copy_(out["terminal_value"], non_blocking=True)
+        ctx.stream.synchronize()
+    e1.record(ctx.stream)
+    torch.cuda.synchronize(ctx.dev)
+    e2e_ms = ctx.max_over_ranks(e0.elapsed_time(e1))
+    return {
+        "value": ctx.world * n * depth * a.steps / (total_ms / 1e3), "ms_per_step": total_ms / a.steps,
+        "launch_ms": total_ms / a.steps, "envs_per_launch": n, "plies_per_launch": depth,
+        "bytes_per_update": 1250 + 2 + 4 + 4 + 1 + 512 / depth, "clocks": clocks,
+        "stats": [0, 0, 0, 0, 0],
+        "e2e": {"value": ctx.world * n * depth * steps / (e2e_ms / 1e3), "unit": "updates/s",
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": n * 4},
+        "gpu_launches": 3 * a.steps,
+        "config": {"workload": f"config5: {n_roots} roots/GPU (seeded setups + 150 random plies) x {k} belief samples, "
+                               f"{depth}-ply uniform rollouts in one launch; per-ply bit-packed masks, terminal values; "
+                               "one step = resample + prime + rollout", "envs_per_gpu": n,
+                   "l2": "n/a: per-launch outputs 3.2 GB/GPU", "parallelism": f"root-sharded x{ctx.world}"},
+        "scaling": "weak", "traffic": None,
+    }
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=2)
+    ap.add_argument("--envs", type=int, default=4096, help="envs per GPU (config 2)")
+    ap.add_argument("--plies-per-launch", type=int, default=8, help="config 4 rollout launch length")
+    ap.add_argument("--e2e-steps", type=int, default=500)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--flush-mib", type=int, default=512)
+    args = ap.parse_args()
+    if args.steps is None:
+        args.steps = {2: 3000, 3: 100, 4: 40, 5: 10}[args.config]
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args, int(os.environ.get("RANK", "0")))
+        return
+
+    ctx = Ctx(args)
+    if args.config in (2, 3):
+        r = run_step_config(ctx, args.config)
+    elif args.config == 4:
+        r = run_traj_config(ctx)
+    else:
+        r = run_search_config(ctx)
+
+    if ctx.rank == 0:
         peak, peak_kind = _peaks()
-        achieved = BYTES_PER_UPDATE * B / (launch_ms / 1e3) / 1e9
-        traffic = None
-        tf = ROOT / "profiles" / "step_kernel_traffic.json"
-        if tf.exists():
-            try:
-                traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch_4096")
-            except Exception:
-                traffic = None
+        achieved = r["bytes_per_update"] * r["envs_per_launch"] * r["plies_per_launch"] / (r["launch_ms"] / 1e3) / 1e9
         line = {
             "metric": METRIC,
-            "value": value,
+            "value": r["value"],
             "unit": "updates/s",
-            "n_gpus": world,
+            "n_gpus": ctx.world,
             "steps": args.steps,
             "warmup": args.warmup,
-            "ms_per_step": launch_ms,
+            "ms_per_step": r["ms_per_step"],
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": r["scaling"],
             "vs_baseline": None,
             "dtype": "u8/int32 state, bf16 infostate",
             "data": "synthetic (Philox setups and actions, no dataset)",
-            "config": {
-                "workload": f"config2: {B} envs/GPU, seeded random setups (pool {POOL}), uniform random legal "
-                            "actions, auto-reset, bf16 [B,488,10,10] infostate (75 live planes rewritten per ply), "
-                            "u8 [B,100,100] mask; one step = one fused-kernel ply over all envs",
-                "envs_per_gpu": B,
-                "parallelism": f"env-sharded x{world}, no step-path collective",
-                "l2": f"flushed between timed steps ({args.flush_mib} MiB write, then {args.flush_mib // 2} MiB read)",
-            },
+            "config": r["config"],
             "roofline": {
                 "bound": "hbm",
                 "achieved": achieved,
                 "peak": peak,
                 "unit": "GB/s",
                 "frac": achieved / peak,
-                "traffic": traffic,
-                "bytes_per_update": BYTES_PER_UPDATE,
-                "peak_source": peak_kind,
+                "traffic": r["traffic"],
+                "bytes_per_update": r["bytes_per_update"],
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+                "kernel": "env_kernel (fused step)",
             },
-            "e2e": {
-                "value": e2e,
-                "unit": "updates/s",
-                "h2d_bytes_per_step": B * 8,
-                "d2h_bytes_per_step": B * (4 + 1 + 2),
-                "steps": e2e_steps,
-            },
-            "gpu_launches": args.steps,
-            "clocks": clocks.summary(),
-            "episode_stats": dict(zip(["finished", "red_wins", "blue_wins", "draws", "sum_lengths"], stats_all)),
+            "e2e": r["e2e"],
+            "gpu_launches": r["gpu_launches"],
+            "clocks": r["clocks"],
+            "episode_stats": dict(zip(["finished", "red_wins", "blue_wins", "draws", "sum_lengths"], r["stats"])),
         }
-        if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(B)
+        if ctx.world == 1 and not args.no_cpu_baseline and args.config == 2:
+            line["cpu_baseline"] = cpu_baseline(args.envs)
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    if ctx.world > 1:
+        ctx.dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -147,6 +147,41 @@ int sb_apply_actions(const sb_state *s, const int64_t *actions, void *stream);
 int sb_step(const sb_state *s, const int64_t *actions, int64_t ply, const sb_policy *policy, int auto_reset,
             const sb_step_out *out, void *stream);
 
+/* north-star: a trajectory ring of n_slots slots; every array is laid out
+ * [n_slots, n, ...] and any pointer may be NULL. */
+typedef struct sb_traj {
+    void *infostate;           /* [T,n,C,10,10], see info_dtype / info_layout */
+    int32_t info_dtype;
+    int32_t info_layout;
+    uint8_t *mask_u8;          /* [T,n,100,100] legal mask of the slot's state */
+    uint8_t *mask_bits;        /* [T,n,1250] bit-packed legal mask of the slot's state */
+    int16_t *action;           /* [T,n] action sampled at the slot's state */
+    float *logprob;            /* [T,n] its log-prob under the policy */
+    float *reward;             /* [T,n] player-0 reward of the slot's transition */
+    uint8_t *done;             /* [T,n] the slot's transition ended the game */
+    int64_t *hash;             /* [T,n] Zobrist hash of the slot's state */
+    int64_t *stats;            /* [5] as sb_step_out.stats */
+    int64_t n_slots;           /* T */
+    int64_t slot0;             /* slot holding the current state */
+} sb_traj;
+
+/* north-star: n_plies plies in one launch, each env's record kept on chip.
+ * n_plies == 0 observes the current state into slot slot0 (observation, mask,
+ * sampled action and log-prob).  Ply p applies the action sampled for slot
+ * (slot0+p) % T, writes reward / done there, auto-resets ended games when
+ * auto_reset != 0, and writes the new state's observation, mask, sampled
+ * action and log-prob into slot (slot0+p+1) % T.  The RNG ply of ply p is
+ * ply + p. */
+int sb_rollout(const sb_state *s, int64_t ply, const sb_policy *policy, int auto_reset, int32_t n_plies,
+               const sb_traj *traj, void *stream);
+
+/* north-star: belief resampling for search.  Sample env e becomes a copy of
+ * root root_of[e] (roots: a state of n_roots envs) whose side-not-to-move has
+ * its unrevealed identities re-dealt uniformly among the assignments
+ * consistent with the side to move's information (moved pieces are never a
+ * Bomb or the Flag).  Chase rings start empty; the hash is recomputed. */
+int sb_belief_resample(const sb_state *roots, const sb_state *samples, const int64_t *root_of, void *stream);
+
 /* north-star: sample an action for every env's current state at `ply`. */
 int sb_sample_actions(const sb_state *s, int64_t ply, const sb_policy *policy, int64_t *actions, float *logprob,
                       void *stream);

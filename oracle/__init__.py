@@ -110,6 +110,7 @@ def lib() -> ctypes.CDLL:
             "or_step": (None, [S, C, vp, i64, i32, i32, vp, vp, vp, vp]),
             "or_bench_rollout": (ctypes.c_int, [S, C, i64, i64, i32, vp, vp]),
             "or_fraction": (ctypes.c_float, [ctypes.c_int32, ctypes.c_int32]),
+            "or_belief_resample": (None, [S, S, vp, C]),
             "or_f32_to_bf16": (ctypes.c_uint16, [ctypes.c_float]),
             "or_logit_noise": (None, [u64, i64, i64, ctypes.c_int32, vp, vp]),
         }
@@ -296,6 +297,11 @@ class OracleState:
         )
         self.ply += 1
         return {"action": taken, "logprob": lp, "reward": rew, "done": done}
+
+    def resample_from(self, roots: "OracleState", root_of) -> None:
+        """Belief resampling: env j becomes root root_of[j] re-dealt (see stratego_oracle.c)."""
+        r = np.ascontiguousarray(root_of, dtype=np.int64).reshape(self.n)
+        lib().or_belief_resample(ctypes.byref(roots._st), ctypes.byref(self._st), _ptr(r), ctypes.byref(self._cfg))
 
     def bench_rollout(self, plies: int, threads: int) -> None:
         """Uniform random rollout with u8 mask + bf16 dense infostate outputs."""
