@@ -57,6 +57,7 @@ constexpr int R_NLEGAL = 164;   // i16 legal moves of the side to move (with the
 constexpr int R_PROPKIND = 166; // u8  policy the cached proposal was drawn with
 constexpr int R_PROPLP = 168;   // f32 log-prob of the cached proposal
 constexpr int R_HIST = 176;     // i16[32] move-history ring
+constexpr int R_BLOOM = 240;    // u64[2] per-side Bloom filter of the chase ring's hashes
 
 constexpr uint8_t C_PIECE = 15, C_BLUE = 16, C_OCC = 32, C_MOVED = 64, C_REV = 128;
 
@@ -84,8 +85,9 @@ __device__ __forceinline__ bool is_lake(int sq) {
 __device__ __forceinline__ bool can_move(int pt) { return pt >= 1 && pt <= 10; }
 __device__ __forceinline__ int owner_of(uint8_t c) { return (c & C_OCC) ? ((c >> 4) & 1) : -1; }
 
+// Zobrist entry [sq][owner][piece] of a [10,10,2,13] table (global or shared).
 __device__ __forceinline__ uint64_t zob(const int64_t* z, int sq, int owner, int piece) {
-    return (uint64_t)__ldg(z + (sq * 2 + owner) * 13 + piece);
+    return (uint64_t)z[(sq * 2 + owner) * 13 + piece];
 }
 
 // Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11).
@@ -136,6 +138,24 @@ __device__ __forceinline__ void bulk_s2g(void* gdst, const void* ssrc, uint32_t 
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders completed async-proxy (bulk copy) writes to global memory before
+// later generic-proxy stores to the same bytes.
+__device__ __forceinline__ void fence_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Named CTA barriers (ids 1-15; 0 is __syncthreads): sync waits, arrive
+// only counts in; nthreads is the total of both sides, a multiple of 32.
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+__device__ __forceinline__ void named_arrive(int id, int nthreads) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Three bits of a Zobrist hash in a 64-bit Bloom filter (the hash bits are
+// uniformly random, so its low 18 bits serve as three independent indices).
+__device__ __forceinline__ uint64_t bloom_bits(uint64_t h) {
+    return (1ull << (h & 63)) | (1ull << ((h >> 6) & 63)) | (1ull << ((h >> 12) & 63));
+}
 
 }  // namespace sb

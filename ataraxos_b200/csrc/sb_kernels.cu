@@ -83,11 +83,14 @@ struct KArgs {
     int64_t slot0;
 };
 
-constexpr int WARPS = 4;  // warps (envs in flight) per CTA
+constexpr int WARPS = 8;  // warps (envs in flight) per CTA
+constexpr int ZOB_N = 2600;  // entries of the [10,10,2,13] Zobrist table
 constexpr int SM_RAYS = 256;
 constexpr int SM_PAT_OPP = 512;
 constexpr int SM_PAT_OWN = 912;
-constexpr int SM_FIXED = 1312;
+constexpr int SM_ACTS = 1312;  // 256 x int16 legal-action list (Gumbel sampling)
+constexpr int SM_FIXED = 1824;
+constexpr int ZERO_BYTES = 12800;  // per-CTA zero buffer, source of the bulk zero fills
 
 // ---------------------------------------------------------------------------
 // Legal moves
@@ -192,7 +195,7 @@ __device__ __forceinline__ void logit_noise(uint64_t seed, int64_t ge, int64_t p
 // of logit + Gumbel over legal actions, ties to the smaller action index.
 template <int POL>
 __device__ void choose(const KArgs& a, const uint16_t* rays, const int cnt[4], int n, int64_t e, int64_t ply,
-                       int lane, int& act, float& lp) {
+                       int lane, int& act, float& lp, int16_t* acts = nullptr) {
     const int64_t ge = a.env_base + e;
     if (n == 0) {
         act = -1;
@@ -208,28 +211,53 @@ __device__ void choose(const KArgs& a, const uint16_t* rays, const int cnt[4], i
     }
     float best = -INFINITY, bestz = 0.0f, m = -INFINITY, s = 0.0f;
     int besta = 0x7fffffff;
+    auto visit = [&](int ac) {
+        float z, g;
+        logit_noise(a.seed, ge, ply, ac, z, g);
+        if (a.logits) z = a.logits[e * NACT + ac];
+        const float key = z + g;
+        if (key > best || (key == best && ac < besta)) {
+            best = key;
+            besta = ac;
+            bestz = z;
+        }
+        if (z > m) {
+            s = s * expf(m - z) + 1.0f;
+            m = z;
+        } else {
+            s += expf(z - m);
+        }
+    };
+    if (acts && n <= 256) {
+        // spread the legal actions evenly over the lanes: list them in
+        // ascending order in shared memory, then lane i takes i, i+32, ...
+        int base = 0;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int sq = lane + 32 * k;
-        if (sq >= NSQ || cnt[k] == 0) continue;
-        const uint32_t r = rays[sq];
-        for (int j = 0; j < cnt[k]; ++j) {
-            const int ac = sq * 100 + decode_ray(sq, r, j);
-            float z, g;
-            logit_noise(a.seed, ge, ply, ac, z, g);
-            if (a.logits) z = a.logits[e * NACT + ac];
-            const float key = z + g;
-            if (key > best || (key == best && ac < besta)) {
-                best = key;
-                besta = ac;
-                bestz = z;
+        for (int k = 0; k < 4; ++k) {
+            const int c = cnt[k];
+            int incl = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(FULL, incl, o);
+                if (lane >= o) incl += v;
             }
-            if (z > m) {
-                s = s * expf(m - z) + 1.0f;
-                m = z;
-            } else {
-                s += expf(z - m);
+            const int sq = lane + 32 * k;
+            if (c) {
+                const uint32_t r = rays[sq];
+                const int pos = base + incl - c;
+                for (int j = 0; j < c; ++j) acts[pos + j] = (int16_t)(sq * 100 + decode_ray(sq, r, j));
             }
+            base += __shfl_sync(FULL, incl, 31);
+        }
+        __syncwarp();
+        for (int i = lane; i < n; i += 32) visit(acts[i]);
+        __syncwarp();
+    } else {
+        for (int k = 0; k < 4; ++k) {
+            const int sq = lane + 32 * k;
+            if (sq >= NSQ || cnt[k] == 0) continue;
+            const uint32_t r = rays[sq];
+            for (int j = 0; j < cnt[k]; ++j) visit(sq * 100 + decode_ray(sq, r, j));
         }
     }
 #pragma unroll
@@ -256,7 +284,9 @@ __device__ void choose(const KArgs& a, const uint16_t* rays, const int cnt[4], i
 // Reset (csrc/stratego_buffer.cu:529-618; host part cpp:289-291)
 // ---------------------------------------------------------------------------
 
-__device__ void reset_env(uint8_t* rec, int64_t* ring2, const KArgs& a, int64_t e, bool from_pool, int lane) {
+// zt: the Zobrist table (the CTA's shared-memory copy in env_kernel).
+__device__ void reset_env(uint8_t* rec, int64_t* ring2, const KArgs& a, const int64_t* zt, int64_t e, bool from_pool,
+                          int lane) {
     const uint8_t* red = nullptr;
     const uint8_t* blue = nullptr;
     const int32_t ep = fld<int32_t>(rec, R_EPISODE);
@@ -287,13 +317,13 @@ __device__ void reset_env(uint8_t* rec, int64_t* ring2, const KArgs& a, int64_t 
             if (rp < 0 || rp > 12) bad = true;
             else {
                 code = (uint8_t)(rp | C_OCC);
-                h ^= zob(a.zob, sq, 0, rp);
+                h ^= zob(zt, sq, 0, rp);
             }
         } else if (bp != 0) {
             if (bp < 0 || bp > 12) bad = true;
             else {
                 code = (uint8_t)(bp | C_OCC | C_BLUE);
-                h ^= zob(a.zob, sq, 1, bp);
+                h ^= zob(zt, sq, 1, bp);
             }
         }
         rec[sq] = code;
@@ -334,6 +364,8 @@ __device__ void reset_env(uint8_t* rec, int64_t* ring2, const KArgs& a, int64_t 
         fld<int32_t>(rec, R_PROPPLY) = -1;
         fld<int16_t>(rec, R_NLEGAL) = 0;
         fld<float>(rec, R_PROPLP) = 0.0f;
+        fld<uint64_t>(rec, R_BLOOM) = 0;
+        fld<uint64_t>(rec, R_BLOOM + 8) = 0;
     }
     __syncwarp();
 }
@@ -346,10 +378,10 @@ __device__ void reset_env(uint8_t* rec, int64_t* ring2, const KArgs& a, int64_t 
 // success the board, counters, history, trackers and the caps part of the
 // terminal check are done; check_legal asks the caller for the "side to move
 // has no legal move" test on the new board.
-// ring_lo / ring_hi: this lane's prefetched entries lane and lane+32 of the
-// mover's chase ring (valid below the ring length).
-__device__ bool apply_env(uint8_t* rec, int64_t* ring2, const KArgs& a, int64_t act, int lane, uint64_t ring_lo,
-                          uint64_t ring_hi, bool& check_legal, bool& flag_taken) {
+// The chase ring is read only when the mover's Bloom filter of its hashes
+// (R_BLOOM, cleared with the ring) says the new hash may be in it.
+__device__ bool apply_env(uint8_t* rec, int64_t* ring2, const KArgs& a, const int64_t* zt, int64_t act, int lane,
+                          bool& check_legal, bool& flag_taken) {
     check_legal = false;
     flag_taken = false;
     if (act < 0 || act >= NACT) return false;
@@ -399,10 +431,10 @@ __device__ bool apply_env(uint8_t* rec, int64_t* ring2, const KArgs& a, int64_t 
     else if (result == 2) dpart = (uint8_t)(cd & (C_PIECE | C_BLUE | C_OCC));
     const uint8_t ns = fs, nd = (uint8_t)(fd | dpart);
 
-    uint64_t h = fld<uint64_t>(rec, R_ZHASH) ^ zob(a.zob, src, p, ps);
-    if (result == 0) h ^= zob(a.zob, dst, p, ps);
-    else if (result == 1) h ^= zob(a.zob, dst, opp, pd) ^ zob(a.zob, dst, p, ps);
-    else if (result == 3) h ^= zob(a.zob, dst, opp, pd);
+    uint64_t h = fld<uint64_t>(rec, R_ZHASH) ^ zob(zt, src, p, ps);
+    if (result == 0) h ^= zob(zt, dst, p, ps);
+    else if (result == 1) h ^= zob(zt, dst, opp, pd) ^ zob(zt, dst, p, ps);
+    else if (result == 3) h ^= zob(zt, dst, opp, pd);
 
     const int32_t msa = attack ? 0 : fld<int32_t>(rec, R_MSA) + 1;
     const int32_t mn = fld<int32_t>(rec, R_MOVENUM) + 1;
@@ -442,11 +474,17 @@ __device__ bool apply_env(uint8_t* rec, int64_t* ring2, const KArgs& a, int64_t 
         if ((c & C_OCC) && ((c >> 4) & 1) == opp) threat = true;
     }
     int chh = rec[R_CHHEAD + p], chl = rec[R_CHLEN + p], chlast = fld<int8_t>(rec, R_CHLAST + p);
+    uint64_t bloom = fld<uint64_t>(rec, R_BLOOM + 8 * p);
     uint8_t chv = rec[R_CHVIOL];
     int64_t* ring = ring2 + p * NRING;
     if (threat) {
-        const bool f = (lane < chl && ring_lo == h) || (lane + 32 < chl && ring_hi == h);
-        const bool found = __any_sync(FULL, f);
+        const uint64_t bb = bloom_bits(h);
+        bool found = false;
+        if ((bloom & bb) == bb) {
+            const bool f = (lane < chl && (uint64_t)ring[lane] == h) || (lane + 32 < chl && (uint64_t)ring[lane + 32] == h);
+            found = __any_sync(FULL, f);
+        }
+        bloom |= bb;
         const bool exc = chlast >= 0 && dst == chlast;
         if (found && !exc) chv = 1;
         if (lane == 0) ring[chl < NRING ? chl : chh] = (int64_t)h;
@@ -457,6 +495,7 @@ __device__ bool apply_env(uint8_t* rec, int64_t* ring2, const KArgs& a, int64_t 
         chl = 0;
         chh = 0;
         chlast = -1;
+        bloom = 0;
     }
 
     // terminal caps (cu:383-395); the legal-move test is the caller's
@@ -483,6 +522,7 @@ __device__ bool apply_env(uint8_t* rec, int64_t* ring2, const KArgs& a, int64_t 
         rec[R_CHHEAD + p] = (uint8_t)chh;
         rec[R_CHLEN + p] = (uint8_t)chl;
         fld<int8_t>(rec, R_CHLAST + p) = (int8_t)chlast;
+        fld<uint64_t>(rec, R_BLOOM + 8 * p) = bloom;
         rec[R_CHVIOL] = chv;
         fld<int8_t>(rec, R_OUTCOME) = outcome;
         rec[R_TERM] = outcome != -1;
@@ -534,14 +574,28 @@ __device__ __forceinline__ void zero_chunks(uint8_t* g, int nchunks, int lane) {
     for (int i = lane; i < nchunks; i += 32) st16(g + i * 16, Z);
 }
 
-// Background of the infostate (stratego/env/infostate.py:37-109): the rows
-// of hidden-piece probabilities (channels 12-23 opponent, 24-35 own), the
-// constant planes 41/42, zeros elsewhere; channels 456-487 zeroed.  The
-// 400-byte hidden-piece row (two bf16 planes or one f32 plane) is built in
-// shared memory and lanes 0-24 each replicate one 16-byte column of it.
+// State-independent zero rows of one env's infostate: channels 0-11, 36-40
+// (up to the 16-byte chunk shared with channel 41), 456-487, and 43-455
+// when every channel is written (SB_LAYOUT_DENSE_ALL).
 template <typename T>
-__device__ void info_background(const uint8_t* rec, const KArgs& a, int lane, uint8_t* g, int hist_off, bool all,
-                                T* pat_opp, T* pat_own) {
+__device__ __forceinline__ void info_zeros(int lane, uint8_t* g, int hist_off, bool all) {
+    using G = InfoGeom<T>;
+    constexpr int PB = G::PB;
+    constexpr int C41 = 41 * PB / 16;  // first chunk touching plane 41
+    zero_chunks(g, 12 * PB / 16, lane);
+    zero_chunks(g + 36 * PB, C41 - 36 * PB / 16, lane);
+    zero_chunks(g + hist_off, G::HB / 16, lane);
+    if (all) zero_chunks(g + G::R1B, (456 * PB - G::R1B) / 16, lane);
+}
+
+// State-dependent background of the infostate (stratego/env/infostate.py:
+// 37-109): the rows of hidden-piece probabilities (channels 12-23 opponent,
+// 24-35 own) and the constant planes 41/42.  The 400-byte hidden-piece row
+// (two bf16 planes or one f32 plane) is built in shared memory and lanes 0-24
+// each replicate one 16-byte column of it.
+template <typename T>
+__device__ void info_background(const uint8_t* rec, const KArgs& a, int lane, uint8_t* g, int hist_off, T* pat_opp,
+                                T* pat_own) {
     using G = InfoGeom<T>;
     constexpr int PB = G::PB;
     constexpr int REPS = 12 * PB / 400;
@@ -574,8 +628,6 @@ __device__ void info_background(const uint8_t* rec, const KArgs& a, int lane, ui
             st16(gw + r * 400, vw);
         }
     }
-    zero_chunks(g, 12 * PB / 16, lane);
-    zero_chunks(g + 36 * PB, C41 - 36 * PB / 16, lane);
     const int mn = fld<int32_t>(rec, R_MOVENUM), msa = fld<int32_t>(rec, R_MSA);
     const T v41 = IV<T>::from(a.max_len > 0 ? __fdiv_rn((float)mn, (float)a.max_len) : 0.0f);
     const T v42 = IV<T>::from(a.no_attack_limit > 0 ? __fdiv_rn((float)msa, (float)a.no_attack_limit) : 0.0f);
@@ -588,8 +640,27 @@ __device__ void info_background(const uint8_t* rec, const KArgs& a, int lane, ui
         }
         st16(g + i * 16, ch.v);
     }
-    zero_chunks(g + hist_off, G::HB / 16, lane);
-    if (all) zero_chunks(g + G::R1B, (456 * PB - G::R1B) / 16, lane);
+}
+
+// The state-independent zero regions of one env's outputs, streamed from
+// the CTA's zero buffer by the TMA engine (bulk copies, no multicast) while
+// the warp works on the game logic: the whole u8 mask row and the infostate
+// zero rows of info_zeros().  Issued by one lane; completion is awaited
+// (bulk_wait_all + proxy fence) before the one-hot values are stored on top.
+template <typename T>
+__device__ void bulk_zero_outputs(const uint8_t* zb, uint8_t* gmask, uint8_t* ginfo, int hist_off, bool all) {
+    using G = InfoGeom<T>;
+    constexpr int PB = G::PB;
+    if (gmask) bulk_s2g(gmask, zb, NACT);
+    if (ginfo) {
+        bulk_s2g(ginfo, zb, 12 * PB);
+        bulk_s2g(ginfo + 36 * PB, zb, (41 * PB / 16) * 16 - 36 * PB);
+        bulk_s2g(ginfo + hist_off, zb, G::HB);
+        if (all)
+            for (int off = G::R1B; off < 456 * PB; off += ZERO_BYTES)
+                bulk_s2g(ginfo + off, zb, (uint32_t)min(ZERO_BYTES, 456 * PB - off));
+    }
+    bulk_commit();
 }
 
 // One-hot values of channels 0-11, 24-40 and the +1/-1 of 456-487.
@@ -678,12 +749,18 @@ constexpr int SM_BITS = SM_FIXED;
 // MODE: MODE_GENERIC takes every decision from a.flags; the step modes fix
 // apply + step + propose (and the policy) at compile time so that the hot
 // kernel carries only the code it runs.
-constexpr int MODE_GENERIC = 0, MODE_STEP_UNIFORM = 1, MODE_STEP_GUMBEL = 2;
+constexpr int MODE_GENERIC = 0, MODE_STEP_UNIFORM = 1, MODE_STEP_GUMBEL = 2, MODE_STEP_PROD = 3;
+// MODE_STEP_PROD is MODE_STEP_UNIFORM for one ply with a u8 mask and / or an
+// infostate: its CTAs give up one env warp for a producer warp that streams
+// the zero rows (measured faster for that case; slower for multi-ply and
+// Gumbel launches, whose game logic wants every warp).
 
 template <typename T, int MODE>
-__global__ void __launch_bounds__(WARPS * 32, 8) env_kernel(const KArgs a) {
+__global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
     constexpr bool kStep = MODE != MODE_GENERIC;
-    constexpr int kPol = MODE == MODE_STEP_UNIFORM ? SB_POLICY_UNIFORM : (MODE == MODE_STEP_GUMBEL ? SB_POLICY_GUMBEL : -1);
+    constexpr bool kProd = MODE == MODE_STEP_PROD;
+    constexpr int kPol = (MODE == MODE_STEP_UNIFORM || kProd) ? SB_POLICY_UNIFORM
+                         : (MODE == MODE_STEP_GUMBEL ? SB_POLICY_GUMBEL : -1);
     auto has = [&](uint32_t f) -> bool {
         if (kStep) {
             if (f & (F_RESET_PLANES | F_RESET_POOL | F_SAMPLE_OUT | F_HAS_LEGAL)) return false;
@@ -693,45 +770,101 @@ __global__ void __launch_bounds__(WARPS * 32, 8) env_kernel(const KArgs a) {
         return (a.flags & f) != 0;
     };
     extern __shared__ __align__(128) uint8_t smem[];
-    const int lane = threadIdx.x & 31;
-    uint8_t* ws = smem + (threadIdx.x >> 5) * a.sm_warp;
+    __shared__ __align__(16) int64_t s_zob[ZOB_N];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    // step modes: warps 0..WARPS-2 play one env each; the last warp is the
+    // producer that streams those envs' zero rows with bulk copies and tells
+    // the env warps (named barrier 1) when they are complete.  Barrier 2
+    // tells the producer the env warps' one-hot stores of a ply are issued
+    // before it zeroes the next ply's slots.
+    constexpr int ENVW = kProd ? WARPS - 1 : WARPS;
+    const bool producer = kProd && w == WARPS - 1;
+    // a CTA-wide zero buffer (source of the bulk zero fills) precedes the
+    // warps' regions in the step modes
+    uint8_t* zb = smem;
+    uint8_t* ws = smem + (kProd ? ZERO_BYTES : 0) + w * a.sm_warp;
+    // the Zobrist table lives in shared memory, so that the game logic never
+    // waits on HBM while the outputs stream out
+    for (int i = threadIdx.x; i < ZOB_N / 2; i += blockDim.x)
+        reinterpret_cast<uint4*>(s_zob)[i] = reinterpret_cast<const uint4*>(a.zob)[i];
+    if (kProd) {
+        for (int i = threadIdx.x; i < ZERO_BYTES / 16; i += blockDim.x) st16(zb + i * 16, make_uint4(0, 0, 0, 0));
+        fence_async_smem();
+    }
+    __syncthreads();
     uint8_t* rec = ws;
     uint16_t* rays = reinterpret_cast<uint16_t*>(ws + SM_RAYS);
+    int16_t* acts = reinterpret_cast<int16_t*>(ws + SM_ACTS);
     constexpr int PB = InfoGeom<T>::PB;
     const bool compact = a.info_layout == SB_LAYOUT_COMPACT;
     const int64_t info_env = (int64_t)(compact ? 76 : NCH) * PB;
     const int hist_off = (compact ? 44 : 456) * PB;
     const int np = (kStep && a.n_plies > 1) ? a.n_plies : 1;
-    const int64_t nwarps = (int64_t)gridDim.x * WARPS;
-    for (int64_t e = (int64_t)blockIdx.x * WARPS + (threadIdx.x >> 5); e < a.n; e += nwarps) {
-        reinterpret_cast<uint2*>(rec)[lane] = reinterpret_cast<const uint2*>(a.rec + e * REC)[lane];
-        __syncwarp();
+    const bool zeros = kProd && (has(F_INFO) || has(F_MASK_U8));
+    const int64_t stride = (int64_t)gridDim.x * ENVW;
+    const int64_t first = (int64_t)blockIdx.x * ENVW;
+    const int64_t last_iter = (first < a.n ? (a.n - first + stride - 1) / stride : 0) * np - 1;
+    int64_t iter = 0;
+    for (int64_t base = first; base < a.n; base += stride) {
+        if (producer) {
+            for (int p = 0; p < np; ++p, ++iter) {
+                if (!zeros) continue;
+                if (iter > 0) named_sync(2, WARPS * 32);
+                if (lane == 0) {
+                    // the env warps' plain stores of earlier plies come before
+                    // these bulk writes (a ring of one slot reuses the bytes)
+                    fence_async_global();
+                    const int64_t s_next = has(F_APPLY) ? (a.slot0 + p + 1) % a.n_slots : a.slot0 % a.n_slots;
+                    for (int j = 0; j < ENVW && base + j < a.n; ++j) {
+                        const int64_t in = s_next * a.n + base + j;
+                        bulk_zero_outputs<T>(zb, has(F_MASK_U8) ? a.mask_u8 + in * NACT : nullptr,
+                                             has(F_INFO) ? reinterpret_cast<uint8_t*>(a.info) + in * info_env : nullptr,
+                                             hist_off, a.info_layout == SB_LAYOUT_DENSE_ALL);
+                    }
+                    bulk_wait_all();
+                    fence_async_global();
+                }
+                __syncwarp();
+                named_arrive(1, WARPS * 32);
+            }
+            continue;
+        }
+        const int64_t e = base + w;
+        const bool live = e < a.n;
+        if (live) {
+            reinterpret_cast<uint2*>(rec)[lane] = reinterpret_cast<const uint2*>(a.rec + e * REC)[lane];
+            __syncwarp();
+        }
         int64_t* ring2 = a.ring + e * 2 * NRING;
         bool dirty = false;
         bool rays_ok = false;  // rays/cnt describe the side to move of the current board
         int cnt[4] = {0, 0, 0, 0};
 
-        if ((has(F_RESET_PLANES) || has(F_RESET_POOL)) && (has(F_FORCE) || rec[R_TERM])) {
-            reset_env(rec, ring2, a, e, has(F_RESET_POOL), lane);
+        if (live && (has(F_RESET_PLANES) || has(F_RESET_POOL)) && (has(F_FORCE) || rec[R_TERM])) {
+            reset_env(rec, ring2, a, s_zob, e, has(F_RESET_POOL), lane);
             dirty = true;
         }
 
-        for (int p = 0; p < np; ++p) {
+        for (int p = 0; p < np; ++p, ++iter) {
             const int64_t ply = a.ply + p;
             const int64_t s_cur = (a.slot0 + p) % a.n_slots;
             const int64_t s_next = has(F_APPLY) ? (a.slot0 + p + 1) % a.n_slots : a.slot0 % a.n_slots;
             const int64_t ic = s_cur * a.n + e, in = s_next * a.n + e;
+            uint8_t* ginfo = has(F_INFO) ? reinterpret_cast<uint8_t*>(a.info) + in * info_env : nullptr;
+          if (live) {
+            struct {
+                bool valid = false, term = false, ended = false;
+                int8_t oc = -1;
+                int64_t act = -1;
+                float lp = 0.0f;
+                int32_t len = 0;
+            } tr;
             if (has(F_APPLY)) {
                 const bool was_term = rec[R_TERM] != 0;
                 int64_t act = -1;
                 float lp = 0.0f;
                 if (!was_term) {
-                    // the mover's chase ring, fetched early (used on threatening moves)
                     const int pm = rec[R_PLAYER];
-                    const int rl = rec[R_CHLEN + pm];
-                    const int64_t* ringm = ring2 + pm * NRING;
-                    const uint64_t ring_lo = lane < rl ? (uint64_t)ringm[lane] : 0;
-                    const uint64_t ring_hi = lane + 32 < rl ? (uint64_t)ringm[lane + 32] : 0;
                     int n_legal = -1;
                     if (a.actions) act = a.actions[e];
                     if (!a.actions || has(F_STEP)) {
@@ -747,7 +880,7 @@ __global__ void __launch_bounds__(WARPS * 32, 8) env_kernel(const KArgs a) {
                             n_legal = count_of(cnt);
                             if (!a.actions) {
                                 int ac;
-                                choose<kPol>(a, rays, cnt, n_legal, e, ply, lane, ac, lp);
+                                choose<kPol>(a, rays, cnt, n_legal, e, ply, lane, ac, lp, acts);
                                 act = ac;
                             }
                         }
@@ -764,7 +897,7 @@ __global__ void __launch_bounds__(WARPS * 32, 8) env_kernel(const KArgs a) {
                         __syncwarp();
                     } else {
                         bool chk, flag;
-                        const bool ok = apply_env(rec, ring2, a, act, lane, ring_lo, ring_hi, chk, flag);
+                        const bool ok = apply_env(rec, ring2, a, s_zob, act, lane, chk, flag);
                         if (ok) rays_ok = false;  // the board changed
                         if (!ok) {
                             if (lane == 0) fld<int32_t>(rec, R_INVALID) += 1;
@@ -783,24 +916,20 @@ __global__ void __launch_bounds__(WARPS * 32, 8) env_kernel(const KArgs a) {
                     }
                 }
                 const bool term = rec[R_TERM] != 0;
-                if (lane == 0) {
-                    if (term) fld<int32_t>(rec, R_TSINCE) += 1;
-                    const int8_t oc = fld<int8_t>(rec, R_OUTCOME);
-                    if (a.reward) a.reward[ic] = oc == 0 ? 1.0f : (oc == 1 ? -1.0f : 0.0f);
-                    if (a.done) a.done[ic] = term ? 1 : 0;
-                    if (a.action_taken) a.action_taken[ic] = act;
-                    if (a.logprob_taken) a.logprob_taken[ic] = lp;
-                    if (a.stats && term && !was_term) {
-                        atomicAdd(reinterpret_cast<unsigned long long*>(&a.stats[0]), 1ull);
-                        atomicAdd(reinterpret_cast<unsigned long long*>(&a.stats[oc == 0 ? 1 : (oc == 1 ? 2 : 3)]), 1ull);
-                        atomicAdd(reinterpret_cast<unsigned long long*>(&a.stats[4]),
-                                  (unsigned long long)fld<int32_t>(rec, R_MOVENUM));
-                    }
-                }
+                if (lane == 0 && term) fld<int32_t>(rec, R_TSINCE) += 1;
+                // the transition's outputs are stored at the end of the ply, so
+                // the game logic never waits behind the output stream
+                tr.valid = true;
+                tr.oc = fld<int8_t>(rec, R_OUTCOME);
+                tr.term = term;
+                tr.ended = term && !was_term;
+                tr.act = act;
+                tr.lp = lp;
+                tr.len = fld<int32_t>(rec, R_MOVENUM);
                 __syncwarp();
                 dirty = true;
                 if (has(F_AUTO_RESET) && term) {
-                    reset_env(rec, ring2, a, e, true, lane);
+                    reset_env(rec, ring2, a, s_zob, e, true, lane);
                     rays_ok = false;
                 }
             }
@@ -813,18 +942,19 @@ __global__ void __launch_bounds__(WARPS * 32, 8) env_kernel(const KArgs a) {
                 n = count_of(cnt);
             }
             // background rows of the outputs, then (after one __syncwarp) the one-hots
-            uint8_t* ginfo = nullptr;
-            if (has(F_INFO)) {
-                ginfo = reinterpret_cast<uint8_t*>(a.info) + in * info_env;
-                info_background<T>(rec, a, lane, ginfo, hist_off, a.info_layout == SB_LAYOUT_DENSE_ALL,
-                                   reinterpret_cast<T*>(ws + SM_PAT_OPP), reinterpret_cast<T*>(ws + SM_PAT_OWN));
-            }
-            if (has(F_MASK_U8)) mask_background(a.mask_u8 + in * NACT, lane);
+            // zero rows: streamed by the producer warp since the start of the ply
+            // in MODE_STEP_PROD; plain 16-byte stores issued here otherwise
+            // (after the game logic: issuing them earlier measured slower)
+            if (!kProd && has(F_INFO)) info_zeros<T>(lane, ginfo, hist_off, a.info_layout == SB_LAYOUT_DENSE_ALL);
+            if (!kProd && has(F_MASK_U8)) mask_background(a.mask_u8 + in * NACT, lane);
+            if (has(F_INFO))
+                info_background<T>(rec, a, lane, ginfo, hist_off, reinterpret_cast<T*>(ws + SM_PAT_OPP),
+                                   reinterpret_cast<T*>(ws + SM_PAT_OWN));
             if (has(F_PROPOSE) || has(F_SAMPLE_OUT)) {
                 const int64_t pp = has(F_PROPOSE) ? (has(F_APPLY) ? ply + 1 : ply) : a.ply;
                 int ac;
                 float lp;
-                choose<kPol>(a, rays, cnt, n, e, pp, lane, ac, lp);
+                choose<kPol>(a, rays, cnt, n, e, pp, lane, ac, lp, acts);
                 if (lane == 0) {
                     if (has(F_PROPOSE)) {
                         fld<int16_t>(rec, R_PROP) = (int16_t)ac;
@@ -845,16 +975,34 @@ __global__ void __launch_bounds__(WARPS * 32, 8) env_kernel(const KArgs a) {
             if (lane == 0) {
                 if (has(F_HAS_LEGAL)) a.has_legal[e] = n > 0;
                 if (has(F_HASH)) a.hash[in] = fld<int64_t>(rec, R_ZHASH);
+                if (tr.valid) {
+                    if (a.reward) a.reward[ic] = tr.oc == 0 ? 1.0f : (tr.oc == 1 ? -1.0f : 0.0f);
+                    if (a.done) a.done[ic] = tr.term ? 1 : 0;
+                    if (a.action_taken) a.action_taken[ic] = tr.act;
+                    if (a.logprob_taken) a.logprob_taken[ic] = tr.lp;
+                    if (a.stats && tr.ended) {
+                        atomicAdd(reinterpret_cast<unsigned long long*>(&a.stats[0]), 1ull);
+                        atomicAdd(reinterpret_cast<unsigned long long*>(&a.stats[tr.oc == 0 ? 1 : (tr.oc == 1 ? 2 : 3)]),
+                                  1ull);
+                        atomicAdd(reinterpret_cast<unsigned long long*>(&a.stats[4]), (unsigned long long)tr.len);
+                    }
+                }
             }
             __syncwarp();
+          }
+            // the zero rows of this ply's slots are complete (producer warp)
+            if (zeros) named_sync(1, WARPS * 32);
+          if (live) {
             if (has(F_MASK_U8)) mask_scatter(rays, lane, a.mask_u8 + in * NACT);
             if (has(F_MASK_BITS))
                 mask_bits(rays, lane, reinterpret_cast<uint32_t*>(ws + SM_BITS), a.mask_bits + in * SB_MASK_BITS_BYTES);
             if (has(F_INFO)) info_scatter<T>(rec, lane, ginfo, hist_off);
             __syncwarp();
+          }
+            if (zeros && iter < last_iter) named_arrive(2, WARPS * 32);
         }
 
-        if (dirty) reinterpret_cast<uint2*>(a.rec + e * REC)[lane] = reinterpret_cast<const uint2*>(rec)[lane];
+        if (live && dirty) reinterpret_cast<uint2*>(a.rec + e * REC)[lane] = reinterpret_cast<const uint2*>(rec)[lane];
         __syncwarp();
     }
 }
@@ -958,6 +1106,8 @@ __global__ void __launch_bounds__(WARPS * 32) belief_kernel(const uint8_t* root_
             fld<int8_t>(rec, R_CHLAST + 1) = -1;
             fld<int32_t>(rec, R_PROPPLY) = -1;
             fld<int16_t>(rec, R_PROP) = -1;
+            fld<uint64_t>(rec, R_BLOOM) = 0;
+            fld<uint64_t>(rec, R_BLOOM + 8) = 0;
         }
         __syncwarp();
         uint64_t h = 0;
@@ -1166,7 +1316,11 @@ int blocks_per_sm(const void* fn, int dev, int smem, int* out) {
         int optin = 0;
         cudaError_t e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
         if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
-        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+        cudaFuncAttributes fa;
+        e = cudaFuncGetAttributes(&fa, fn);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes");
+        // dynamic shared memory may use what the static part leaves
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
         if (g_nattr < 64) {
             g_attr_fn[g_nattr] = fn;
@@ -1209,11 +1363,12 @@ int launch_mode(sb::KArgs& k, cudaStream_t st) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-    const int smem = sb::WARPS * k.sm_warp;
+    const int smem = (MODE == sb::MODE_STEP_PROD ? sb::ZERO_BYTES : 0) + sb::WARPS * k.sm_warp;
     int nb = 0, sms = 0, rc;
     if ((rc = blocks_per_sm(fn, dev, smem, &nb)) != SB_OK) return rc;
     if ((rc = sm_count(dev, &sms)) != SB_OK) return rc;
-    int64_t blocks = (k.n + sb::WARPS - 1) / sb::WARPS;
+    const int envw = MODE == sb::MODE_STEP_PROD ? sb::WARPS - 1 : sb::WARPS;
+    int64_t blocks = (k.n + envw - 1) / envw;
     const int64_t cap = (int64_t)sms * nb;
     if (blocks > cap) blocks = cap;
     sb::env_kernel<T, MODE><<<(unsigned)blocks, sb::WARPS * 32, smem, st>>>(k);
@@ -1230,14 +1385,19 @@ int launch_env(sb::KArgs& k, int dtype, cudaStream_t st) {
     const uint32_t step = sb::F_APPLY | sb::F_STEP | sb::F_PROPOSE;
     const uint32_t off = sb::F_RESET_PLANES | sb::F_RESET_POOL | sb::F_SAMPLE_OUT | sb::F_HAS_LEGAL;
     int mode = sb::MODE_GENERIC;
-    if ((k.flags & step) == step && !(k.flags & off))
+    if ((k.flags & step) == step && !(k.flags & off)) {
         mode = k.policy == SB_POLICY_UNIFORM ? sb::MODE_STEP_UNIFORM : sb::MODE_STEP_GUMBEL;
+        if (mode == sb::MODE_STEP_UNIFORM && k.n_plies == 1 && (k.flags & (sb::F_INFO | sb::F_MASK_U8)))
+            mode = sb::MODE_STEP_PROD;
+    }
     const bool f32 = dtype == SB_DTYPE_F32;
     switch (mode) {
         case sb::MODE_STEP_UNIFORM:
             return f32 ? launch_mode<float, sb::MODE_STEP_UNIFORM>(k, st) : launch_mode<uint16_t, sb::MODE_STEP_UNIFORM>(k, st);
         case sb::MODE_STEP_GUMBEL:
             return f32 ? launch_mode<float, sb::MODE_STEP_GUMBEL>(k, st) : launch_mode<uint16_t, sb::MODE_STEP_GUMBEL>(k, st);
+        case sb::MODE_STEP_PROD:
+            return f32 ? launch_mode<float, sb::MODE_STEP_PROD>(k, st) : launch_mode<uint16_t, sb::MODE_STEP_PROD>(k, st);
         default:
             return f32 ? launch_mode<float, sb::MODE_GENERIC>(k, st) : launch_mode<uint16_t, sb::MODE_GENERIC>(k, st);
     }
