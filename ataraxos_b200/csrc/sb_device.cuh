@@ -136,11 +136,10 @@ __device__ __forceinline__ void bulk_s2g(void* gdst, const void* ssrc, uint32_t 
                  : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-// Orders completed async-proxy (bulk copy) writes to global memory before
-// later generic-proxy stores to the same bytes.
+// Orders async-proxy (bulk copy) and generic-proxy accesses to global memory.
 __device__ __forceinline__ void fence_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+// Makes generic-proxy writes to shared memory visible to later bulk copies.
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Named CTA barriers (ids 1-15; 0 is __syncthreads): sync waits, arrive

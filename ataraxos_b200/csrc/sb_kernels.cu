@@ -85,12 +85,11 @@ struct KArgs {
 
 constexpr int WARPS = 8;  // warps (envs in flight) per CTA
 constexpr int ZOB_N = 2600;  // entries of the [10,10,2,13] Zobrist table
-constexpr int SM_RAYS = 256;
-constexpr int SM_PAT_OPP = 512;
-constexpr int SM_PAT_OWN = 912;
-constexpr int SM_ACTS = 1312;  // 256 x int16 legal-action list (Gumbel sampling)
-constexpr int SM_FIXED = 1824;
-constexpr int ZERO_BYTES = 12800;  // per-CTA zero buffer, source of the bulk zero fills
+constexpr int SM_RAYS = 256;   // 100 x uint16 packed rays
+constexpr int SM_ACTS = 576;   // 256 x int16 legal-action list (Gumbel sampling)
+constexpr int SM_FIXED = 1088;
+constexpr int SM_BITS = SM_FIXED;  // 1264-byte bit-packed legal mask (mask outputs only)
+constexpr int ZERO_BYTES = 12800;  // MODE_STEP_PROD: per-CTA zero buffer, source of the bulk zero rows
 
 // ---------------------------------------------------------------------------
 // Legal moves
@@ -537,11 +536,10 @@ __device__ bool apply_env(uint8_t* rec, int64_t* ring2, const KArgs& a, const in
 // Observations, written straight from registers
 // ---------------------------------------------------------------------------
 //
-// Every output row of an env is contiguous, so each lane writes whole 16-byte
-// chunks of its background (zeros, the hidden-piece 1/12 patterns, the two
-// constant planes) and, after a __syncwarp that orders the warp's stores, the
-// few one-hot values land on top as 1-, 2- or 4-byte stores.  The L2 merges
-// the partial sectors, so HBM sees each output byte written once.
+// Stores cover whole rows wherever the values are dense: one warp store per
+// infostate plane row (25 lanes x 4 elements) and 16-byte chunks for the u8
+// mask.  Scalar 1- or 2-byte stores cost one L2 request each, so they are
+// kept to the sparse one-hots (about 100 per env).
 
 template <typename T>
 struct IV;
@@ -574,132 +572,156 @@ __device__ __forceinline__ void zero_chunks(uint8_t* g, int nchunks, int lane) {
     for (int i = lane; i < nchunks; i += 32) st16(g + i * 16, Z);
 }
 
-// State-independent zero rows of one env's infostate: channels 0-11, 36-40
-// (up to the 16-byte chunk shared with channel 41), 456-487, and 43-455
-// when every channel is written (SB_LAYOUT_DENSE_ALL).
+// Four consecutive elements of one plane row (one lane's squares 4L..4L+3):
+// two words of bf16 bits or four words of f32 bits.
 template <typename T>
-__device__ __forceinline__ void info_zeros(int lane, uint8_t* g, int hist_off, bool all) {
-    using G = InfoGeom<T>;
-    constexpr int PB = G::PB;
-    constexpr int C41 = 41 * PB / 16;  // first chunk touching plane 41
-    zero_chunks(g, 12 * PB / 16, lane);
-    zero_chunks(g + 36 * PB, C41 - 36 * PB / 16, lane);
-    zero_chunks(g + hist_off, G::HB / 16, lane);
-    if (all) zero_chunks(g + G::R1B, (456 * PB - G::R1B) / 16, lane);
+struct Quad;
+template <>
+struct Quad<uint16_t> {
+    using V = uint2;
+    // element pattern `pat` where mask byte j is 0xFF, 0 elsewhere
+    static __device__ __forceinline__ V sel(uint32_t m, uint32_t pat) {
+        const uint32_t p2 = pat | (pat << 16);
+        return make_uint2(__byte_perm(m, 0, 0x1100) & p2, __byte_perm(m, 0, 0x3322) & p2);
+    }
+    static __device__ __forceinline__ V splat(uint32_t pat) {
+        const uint32_t p2 = pat | (pat << 16);
+        return make_uint2(p2, p2);
+    }
+    static __device__ __forceinline__ V orv(V a, V b) { return make_uint2(a.x | b.x, a.y | b.y); }
+    static __device__ __forceinline__ void st(uint8_t* p, V v) { *reinterpret_cast<uint2*>(p) = v; }
+    static __device__ __forceinline__ uint32_t bits(uint16_t v) { return v; }
+};
+template <>
+struct Quad<float> {
+    using V = uint4;
+    static __device__ __forceinline__ V sel(uint32_t m, uint32_t pat) {
+        return make_uint4(__byte_perm(m, 0, 0x0000) & pat, __byte_perm(m, 0, 0x1111) & pat,
+                          __byte_perm(m, 0, 0x2222) & pat, __byte_perm(m, 0, 0x3333) & pat);
+    }
+    static __device__ __forceinline__ V splat(uint32_t pat) { return make_uint4(pat, pat, pat, pat); }
+    static __device__ __forceinline__ V orv(V a, V b) { return make_uint4(a.x | b.x, a.y | b.y, a.z | b.z, a.w | b.w); }
+    static __device__ __forceinline__ void st(uint8_t* p, V v) { *reinterpret_cast<uint4*>(p) = v; }
+    static __device__ __forceinline__ uint32_t bits(float v) { return __float_as_uint(v); }
+};
+
+// Infostate of the side to move (stratego/env/infostate.py:37-109, channel
+// meaning as csrc/stratego_buffer.cu:707-767).  Lanes 0..24 own squares
+// 4L..4L+3: each derives its squares' features as byte vectors and writes
+// its 4-element slice of every plane row, so one warp store covers a whole
+// 100-element row.  The dense planes (12-42) are computed in full with byte
+// SIMD compares; the sparse ones (0-11: one 1 per own piece; 456-487: one +1
+// and one -1 per move) are zero rows plus one scalar store per non-zero.
+// sd: the warp's 32-entry table of (src | dst << 8) of the last moves, most
+// recent first.
+// Per-square features of lane L's squares 4L..4L+3 as byte vectors.
+struct SqFeat {
+    uint32_t ot, ort, owt, fl;  // own type, opponent revealed type, own revealed type, flag bits
+};
+__device__ __forceinline__ SqFeat square_features(const uint8_t* rec, int lane) {
+    const int p = rec[R_PLAYER];
+    const uint32_t codes = *reinterpret_cast<const uint32_t*>(rec + 4 * lane);
+    SqFeat f{0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t c = (codes >> (8 * j)) & 0xFF;
+        const bool occ = c & C_OCC, rev = c & C_REV, mov = c & C_MOVED;
+        const bool own = occ && ((c >> 4) & 1) == (uint32_t)p, opp = occ && !own;
+        const uint32_t pc = c & C_PIECE;
+        f.ot |= (own ? pc : 0u) << (8 * j);
+        f.ort |= (opp && rev ? pc : 0u) << (8 * j);
+        f.owt |= (own && rev ? pc : 0u) << (8 * j);
+        const uint32_t b = (own && !rev ? 1u : 0u) | (opp && !rev ? 2u : 0u) | (!occ ? 4u : 0u) | (own && mov ? 8u : 0u) |
+                           (opp && mov ? 16u : 0u);
+        f.fl |= b << (8 * j);
+    }
+    return f;
 }
 
-// State-dependent background of the infostate (stratego/env/infostate.py:
-// 37-109): the rows of hidden-piece probabilities (channels 12-23 opponent,
-// 24-35 own) and the constant planes 41/42.  The 400-byte hidden-piece row
-// (two bf16 planes or one f32 plane) is built in shared memory and lanes 0-24
-// each replicate one 16-byte column of it.
+// Dense planes 12-42, computed in full (lanes 0..24).
 template <typename T>
-__device__ void info_background(const uint8_t* rec, const KArgs& a, int lane, uint8_t* g, int hist_off, T* pat_opp,
-                                T* pat_own) {
-    using G = InfoGeom<T>;
-    constexpr int PB = G::PB;
-    constexpr int REPS = 12 * PB / 400;
-    constexpr int C41 = 41 * PB / 16;  // first chunk touching plane 41
-    const int p = rec[R_PLAYER];
-    const T TW = IV<T>::from(__fdiv_rn(1.0f, 12.0f)), ZERO = IV<T>::from(0.0f);
-    for (int k = 0; k < 4; ++k) {
-        const int sq = lane + 32 * k;
-        if (sq >= NSQ) break;
-        const uint8_t c = rec[sq];
-        const bool occ = c & C_OCC, rev = c & C_REV;
-        const bool own = occ && ((c >> 4) & 1) == p, opp = occ && !own;
-        const T vo = (opp && !rev) ? TW : ZERO, vw = (own && !rev) ? TW : ZERO;
-        pat_opp[sq] = vo;
-        pat_own[sq] = vw;
-        if (sizeof(T) == 2) {
-            pat_opp[NSQ + sq] = vo;
-            pat_own[NSQ + sq] = vw;
+__device__ void write_info_dense(const uint8_t* rec, const KArgs& a, int lane, uint8_t* g) {
+    if (lane >= 25) return;
+    using Q = Quad<T>;
+    constexpr int PB = InfoGeom<T>::PB;
+    const SqFeat f = square_features(rec, lane);
+    const uint32_t ONE = Q::bits(IV<T>::from(1.0f));
+    const uint32_t TW = Q::bits(IV<T>::from(__fdiv_rn(1.0f, 12.0f)));
+    uint8_t* gl = g + lane * 4 * (int)sizeof(T);
+    // 12-23: opponent, 1/12 where hidden, one-hot where revealed
+    const typename Q::V hid_o = Q::sel(__vcmpne4(f.fl & 0x02020202u, 0u), TW);
+#pragma unroll
+    for (int t = 0; t < 12; ++t)
+        Q::st(gl + (12 + t) * PB, Q::orv(Q::sel(__vcmpeq4(f.ort, (uint32_t)(t + 1) * 0x01010101u), ONE), hid_o));
+    // 24-35: own pieces as the opponent sees them
+    const typename Q::V hid_w = Q::sel(__vcmpne4(f.fl & 0x01010101u, 0u), TW);
+#pragma unroll
+    for (int t = 0; t < 12; ++t)
+        Q::st(gl + (24 + t) * PB, Q::orv(Q::sel(__vcmpeq4(f.owt, (uint32_t)(t + 1) * 0x01010101u), ONE), hid_w));
+    // 36 own hidden, 37 opponent hidden, 38 empty (lakes included), 39 own moved, 40 opponent moved
+#pragma unroll
+    for (int i = 0; i < 5; ++i) Q::st(gl + (36 + i) * PB, Q::sel(__vcmpne4(f.fl & ((1u << i) * 0x01010101u), 0u), ONE));
+    // 41 / 42: the two fractions (exact float32 quotients)
+    const int mn = fld<int32_t>(rec, R_MOVENUM), msa = fld<int32_t>(rec, R_MSA);
+    Q::st(gl + 41 * PB, Q::splat(Q::bits(IV<T>::from(a.max_len > 0 ? __fdiv_rn((float)mn, (float)a.max_len) : 0.0f))));
+    Q::st(gl + 42 * PB,
+          Q::splat(Q::bits(IV<T>::from(a.no_attack_limit > 0 ? __fdiv_rn((float)msa, (float)a.no_attack_limit) : 0.0f))));
+}
+
+// Sparse planes: 0-11 (one 1 per own piece) and 456-487 (the k-th most recent
+// move's +1 at dst, -1 at src).  Their zero rows are written here unless a
+// producer warp already streamed them (kZerosDone); the non-zeros follow.
+// DENSE_ALL also zeroes planes 43-455.
+template <typename T, bool kZerosDone>
+__device__ void write_info_sparse(const uint8_t* rec, int lane, uint8_t* g, int hist_off, bool all) {
+    using Q = Quad<T>;
+    constexpr int PB = InfoGeom<T>::PB;
+    if (lane < 25) {
+        uint8_t* gl = g + lane * 4 * (int)sizeof(T);
+        if (!kZerosDone) {
+            const typename Q::V Z = Q::splat(0u);
+#pragma unroll
+            for (int t = 0; t < 12; ++t) Q::st(gl + t * PB, Z);
+#pragma unroll 8
+            for (int k = 0; k < 32; ++k) Q::st(gl + hist_off + k * PB, Z);
+        }
+        // own one-hots: same lane as its zero row, so program order suffices
+        const SqFeat f = square_features(rec, lane);
+        T* g1 = reinterpret_cast<T*>(g);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t pc = (f.ot >> (8 * j)) & 0xFF;
+            if (pc) g1[(pc - 1) * NSQ + 4 * lane + j] = IV<T>::from(1.0f);
         }
     }
     __syncwarp();
-    if (lane < 25) {
-        const uint4 vo = reinterpret_cast<const uint4*>(pat_opp)[lane];
-        const uint4 vw = reinterpret_cast<const uint4*>(pat_own)[lane];
-        uint8_t* go = g + 12 * PB + lane * 16;
-        uint8_t* gw = g + 24 * PB + lane * 16;
-#pragma unroll
-        for (int r = 0; r < REPS; ++r) {
-            st16(go + r * 400, vo);
-            st16(gw + r * 400, vw);
-        }
+    const int hl = rec[R_HLEN], hh = rec[R_HHEAD];
+    if (lane < hl) {
+        const int act = fld<int16_t>(rec, R_HIST + 2 * ((hh - 1 - lane) & 31));
+        T* hs = reinterpret_cast<T*>(g + hist_off + lane * PB);
+        hs[act % 100] = IV<T>::from(1.0f);
+        hs[act / 100] = IV<T>::from(-1.0f);
     }
-    const int mn = fld<int32_t>(rec, R_MOVENUM), msa = fld<int32_t>(rec, R_MSA);
-    const T v41 = IV<T>::from(a.max_len > 0 ? __fdiv_rn((float)mn, (float)a.max_len) : 0.0f);
-    const T v42 = IV<T>::from(a.no_attack_limit > 0 ? __fdiv_rn((float)msa, (float)a.no_attack_limit) : 0.0f);
-    for (int i = C41 + lane; i < G::R1B / 16; i += 32) {
-        Chunk<T> ch;
-#pragma unroll
-        for (int j = 0; j < 16 / (int)sizeof(T); ++j) {
-            const int pl = (i * 16 + j * (int)sizeof(T)) / PB;
-            ch.e[j] = pl == 41 ? v41 : (pl == 42 ? v42 : ZERO);
-        }
-        st16(g + i * 16, ch.v);
+    if (all) {
+        const uint4 Z = make_uint4(0, 0, 0, 0);
+        for (int i = 43 * PB / 16 + lane; i < 456 * PB / 16; i += 32) st16(g + i * 16, Z);
     }
 }
 
-// The state-independent zero regions of one env's outputs, streamed from
-// the CTA's zero buffer by the TMA engine (bulk copies, no multicast) while
-// the warp works on the game logic: the whole u8 mask row and the infostate
-// zero rows of info_zeros().  Issued by one lane; completion is awaited
-// (bulk_wait_all + proxy fence) before the one-hot values are stored on top.
+// Zero rows of one env's outputs streamed by the TMA engine (bulk copies from
+// the CTA's zero buffer, no multicast): the whole u8 mask row, infostate
+// planes 0-11 and 456-487.  Issued by the producer lane.
 template <typename T>
-__device__ void bulk_zero_outputs(const uint8_t* zb, uint8_t* gmask, uint8_t* ginfo, int hist_off, bool all) {
-    using G = InfoGeom<T>;
-    constexpr int PB = G::PB;
+__device__ void bulk_zero_rows(const uint8_t* zb, uint8_t* gmask, uint8_t* ginfo, int hist_off) {
+    constexpr int PB = InfoGeom<T>::PB;
     if (gmask) bulk_s2g(gmask, zb, NACT);
     if (ginfo) {
         bulk_s2g(ginfo, zb, 12 * PB);
-        bulk_s2g(ginfo + 36 * PB, zb, (41 * PB / 16) * 16 - 36 * PB);
-        bulk_s2g(ginfo + hist_off, zb, G::HB);
-        if (all)
-            for (int off = G::R1B; off < 456 * PB; off += ZERO_BYTES)
-                bulk_s2g(ginfo + off, zb, (uint32_t)min(ZERO_BYTES, 456 * PB - off));
-    }
-    bulk_commit();
-}
-
-// One-hot values of channels 0-11, 24-40 and the +1/-1 of 456-487.
-template <typename T>
-__device__ void info_scatter(const uint8_t* rec, int lane, uint8_t* g, int hist_off) {
-    const int p = rec[R_PLAYER];
-    const T ONE = IV<T>::from(1.0f), NEG = IV<T>::from(-1.0f);
-    T* r1 = reinterpret_cast<T*>(g);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int sq = lane + 32 * k;
-        if (sq >= NSQ) continue;
-        const uint8_t c = rec[sq];
-        const int pc = c & C_PIECE;
-        const bool rev = c & C_REV, mov = c & C_MOVED;
-        if (!(c & C_OCC)) {
-            r1[38 * NSQ + sq] = ONE;
-        } else if (((c >> 4) & 1) == p) {
-            r1[(pc - 1) * NSQ + sq] = ONE;
-            r1[(rev ? 24 + pc - 1 : 36) * NSQ + sq] = ONE;
-            if (mov) r1[39 * NSQ + sq] = ONE;
-        } else {
-            r1[(rev ? 12 + pc - 1 : 37) * NSQ + sq] = ONE;
-            if (mov) r1[40 * NSQ + sq] = ONE;
-        }
-    }
-    const int hl = rec[R_HLEN], hh = rec[R_HHEAD];
-    if (lane < hl) {
-        T* hs = reinterpret_cast<T*>(g + hist_off);
-        const int slot = (hh - 1 - lane) & 31;
-        const int act = fld<int16_t>(rec, R_HIST + 2 * slot);
-        hs[lane * NSQ + act % 100] = ONE;
-        hs[lane * NSQ + act / 100] = NEG;
+        bulk_s2g(ginfo + hist_off, zb, 32 * PB);
     }
 }
 
-// u8 legal mask (csrc/stratego_buffer.cu:448-507): zero rows, then ones.
-__device__ __forceinline__ void mask_background(uint8_t* g, int lane) { zero_chunks(g, NACT / 16, lane); }
-
+// u8 legal-mask ones on top of a zeroed row (MODE_STEP_PROD).
 __device__ void mask_scatter(const uint16_t* rays, int lane, uint8_t* m) {
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -716,8 +738,11 @@ __device__ void mask_scatter(const uint16_t* rays, int lane, uint8_t* m) {
     }
 }
 
-// bit-packed mask: bit j of byte k = flat action 8k+j, built in shared memory.
-__device__ void mask_bits(const uint16_t* rays, int lane, uint32_t* w, uint8_t* g) {
+// Legal mask (csrc/stratego_buffer.cu:448-507) of the side to move, built
+// bit-packed in shared memory from the rays (bit j of byte k = flat action
+// 8k+j), then written as bit-packed rows and / or expanded to u8 rows in
+// whole 16-byte chunks.
+__device__ void build_mask_bits(const uint16_t* rays, int lane, uint32_t* w) {
     for (int i = lane; i < 79; i += 32) reinterpret_cast<uint4*>(w)[i] = make_uint4(0, 0, 0, 0);
     __syncwarp();
 #pragma unroll
@@ -733,6 +758,20 @@ __device__ void mask_bits(const uint16_t* rays, int lane, uint32_t* w, uint8_t* 
         }
     }
     __syncwarp();
+}
+
+__device__ __forceinline__ uint32_t nibble_bytes(uint32_t n) { return (n * 0x00204081u) & 0x01010101u; }
+
+__device__ void write_mask_u8(const uint32_t* w, int lane, uint8_t* g) {
+    const uint16_t* b16 = reinterpret_cast<const uint16_t*>(w);
+    for (int c = lane; c < NACT / 16; c += 32) {
+        const uint32_t b = b16[c];
+        st16(g + c * 16, make_uint4(nibble_bytes(b & 15), nibble_bytes((b >> 4) & 15), nibble_bytes((b >> 8) & 15),
+                                    nibble_bytes(b >> 12)));
+    }
+}
+
+__device__ void write_mask_bits(const uint32_t* w, int lane, uint8_t* g) {
     const uint16_t* src = reinterpret_cast<const uint16_t*>(w);
     uint16_t* dst = reinterpret_cast<uint16_t*>(g);
     for (int i = lane; i < SB_MASK_BITS_BYTES / 2; i += 32) dst[i] = src[i];
@@ -742,18 +781,18 @@ __device__ void mask_bits(const uint16_t* rays, int lane, uint32_t* w, uint8_t* 
 // The per-env kernel
 // ---------------------------------------------------------------------------
 
-// Shared memory per warp: record (256), rays (256), two hidden-piece rows
-// (2 x 400) and, for bit-packed masks only, a 1264-byte bit buffer.
-constexpr int SM_BITS = SM_FIXED;
-
 // MODE: MODE_GENERIC takes every decision from a.flags; the step modes fix
 // apply + step + propose (and the policy) at compile time so that the hot
 // kernel carries only the code it runs.
 constexpr int MODE_GENERIC = 0, MODE_STEP_UNIFORM = 1, MODE_STEP_GUMBEL = 2, MODE_STEP_PROD = 3;
-// MODE_STEP_PROD is MODE_STEP_UNIFORM for one ply with a u8 mask and / or an
-// infostate: its CTAs give up one env warp for a producer warp that streams
-// the zero rows (measured faster for that case; slower for multi-ply and
-// Gumbel launches, whose game logic wants every warp).
+// MODE_STEP_PROD is MODE_STEP_UNIFORM for a single ply with a u8 mask and /
+// or an infostate (the config-2 step).  There every env's game logic runs in
+// one wave at the same time, so HBM would idle through it: each 8-warp CTA
+// gives one warp to a producer that streams the envs' zero rows with bulk
+// copies while the other 7 play; named barrier 1 orders the completed zero
+// rows before the one-hots stored on top, barrier 2 orders the one-hots of a
+// batch before the producer's next bulk writes.  Multi-ply and Gumbel
+// launches keep all 8 warps on envs (measured faster there).
 
 template <typename T, int MODE>
 __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
@@ -772,19 +811,12 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(16) int64_t s_zob[ZOB_N];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    // step modes: warps 0..WARPS-2 play one env each; the last warp is the
-    // producer that streams those envs' zero rows with bulk copies and tells
-    // the env warps (named barrier 1) when they are complete.  Barrier 2
-    // tells the producer the env warps' one-hot stores of a ply are issued
-    // before it zeroes the next ply's slots.
-    constexpr int ENVW = kProd ? WARPS - 1 : WARPS;
+    constexpr int ENVW = kProd ? WARPS - 1 : WARPS;  // warps that play envs
     const bool producer = kProd && w == WARPS - 1;
-    // a CTA-wide zero buffer (source of the bulk zero fills) precedes the
-    // warps' regions in the step modes
-    uint8_t* zb = smem;
+    uint8_t* zb = smem;  // MODE_STEP_PROD: the zero buffer precedes the warps' regions
     uint8_t* ws = smem + (kProd ? ZERO_BYTES : 0) + w * a.sm_warp;
-    // the Zobrist table lives in shared memory, so that the game logic never
-    // waits on HBM while the outputs stream out
+    // the Zobrist table lives in shared memory: the game logic never waits on
+    // HBM for it while the outputs stream out
     for (int i = threadIdx.x; i < ZOB_N / 2; i += blockDim.x)
         reinterpret_cast<uint4*>(s_zob)[i] = reinterpret_cast<const uint4*>(a.zob)[i];
     if (kProd) {
@@ -795,6 +827,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
     uint8_t* rec = ws;
     uint16_t* rays = reinterpret_cast<uint16_t*>(ws + SM_RAYS);
     int16_t* acts = reinterpret_cast<int16_t*>(ws + SM_ACTS);
+    uint32_t* wbits = reinterpret_cast<uint32_t*>(ws + SM_BITS);
     constexpr int PB = InfoGeom<T>::PB;
     const bool compact = a.info_layout == SB_LAYOUT_COMPACT;
     const int64_t info_env = (int64_t)(compact ? 76 : NCH) * PB;
@@ -811,16 +844,16 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                 if (!zeros) continue;
                 if (iter > 0) named_sync(2, WARPS * 32);
                 if (lane == 0) {
-                    // the env warps' plain stores of earlier plies come before
-                    // these bulk writes (a ring of one slot reuses the bytes)
+                    // the env warps' stores of the previous batch come first
                     fence_async_global();
                     const int64_t s_next = has(F_APPLY) ? (a.slot0 + p + 1) % a.n_slots : a.slot0 % a.n_slots;
                     for (int j = 0; j < ENVW && base + j < a.n; ++j) {
                         const int64_t in = s_next * a.n + base + j;
-                        bulk_zero_outputs<T>(zb, has(F_MASK_U8) ? a.mask_u8 + in * NACT : nullptr,
-                                             has(F_INFO) ? reinterpret_cast<uint8_t*>(a.info) + in * info_env : nullptr,
-                                             hist_off, a.info_layout == SB_LAYOUT_DENSE_ALL);
+                        bulk_zero_rows<T>(zb, has(F_MASK_U8) ? a.mask_u8 + in * NACT : nullptr,
+                                          has(F_INFO) ? reinterpret_cast<uint8_t*>(a.info) + in * info_env : nullptr,
+                                          hist_off);
                     }
+                    bulk_commit();
                     bulk_wait_all();
                     fence_async_global();
                 }
@@ -941,15 +974,6 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                 if (!rays_ok) enumerate(rec, rec[R_PLAYER], rays, lane, cnt);
                 n = count_of(cnt);
             }
-            // background rows of the outputs, then (after one __syncwarp) the one-hots
-            // zero rows: streamed by the producer warp since the start of the ply
-            // in MODE_STEP_PROD; plain 16-byte stores issued here otherwise
-            // (after the game logic: issuing them earlier measured slower)
-            if (!kProd && has(F_INFO)) info_zeros<T>(lane, ginfo, hist_off, a.info_layout == SB_LAYOUT_DENSE_ALL);
-            if (!kProd && has(F_MASK_U8)) mask_background(a.mask_u8 + in * NACT, lane);
-            if (has(F_INFO))
-                info_background<T>(rec, a, lane, ginfo, hist_off, reinterpret_cast<T*>(ws + SM_PAT_OPP),
-                                   reinterpret_cast<T*>(ws + SM_PAT_OWN));
             if (has(F_PROPOSE) || has(F_SAMPLE_OUT)) {
                 const int64_t pp = has(F_PROPOSE) ? (has(F_APPLY) ? ply + 1 : ply) : a.ply;
                 int ac;
@@ -989,14 +1013,28 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                 }
             }
             __syncwarp();
+            // outputs of the new state: dense rows first (no zero pass needed)
+            if (has(F_INFO)) write_info_dense<T>(rec, a, lane, ginfo);
           }
-            // the zero rows of this ply's slots are complete (producer warp)
+            // MODE_STEP_PROD: this batch's zero rows are complete (producer)
             if (zeros) named_sync(1, WARPS * 32);
           if (live) {
-            if (has(F_MASK_U8)) mask_scatter(rays, lane, a.mask_u8 + in * NACT);
-            if (has(F_MASK_BITS))
-                mask_bits(rays, lane, reinterpret_cast<uint32_t*>(ws + SM_BITS), a.mask_bits + in * SB_MASK_BITS_BYTES);
-            if (has(F_INFO)) info_scatter<T>(rec, lane, ginfo, hist_off);
+            const bool all = a.info_layout == SB_LAYOUT_DENSE_ALL;
+            if (kProd) {
+                if (has(F_INFO)) write_info_sparse<T, true>(rec, lane, ginfo, hist_off, all);
+                if (has(F_MASK_U8)) mask_scatter(rays, lane, a.mask_u8 + in * NACT);
+                if (has(F_MASK_BITS)) {
+                    build_mask_bits(rays, lane, wbits);
+                    write_mask_bits(wbits, lane, a.mask_bits + in * SB_MASK_BITS_BYTES);
+                }
+            } else {
+                if (has(F_INFO)) write_info_sparse<T, false>(rec, lane, ginfo, hist_off, all);
+                if (has(F_MASK_U8) || has(F_MASK_BITS)) {
+                    build_mask_bits(rays, lane, wbits);
+                    if (has(F_MASK_U8)) write_mask_u8(wbits, lane, a.mask_u8 + in * NACT);
+                    if (has(F_MASK_BITS)) write_mask_bits(wbits, lane, a.mask_bits + in * SB_MASK_BITS_BYTES);
+                }
+            }
             __syncwarp();
           }
             if (zeros && iter < last_iter) named_arrive(2, WARPS * 32);
@@ -1353,7 +1391,7 @@ int sm_count(int dev, int* out) {
 // the bit buffer of bit-packed masks.
 void plan_smem(sb::KArgs& k) {
     int off = sb::SM_FIXED;
-    if (k.flags & sb::F_MASK_BITS) off += 1264;
+    if (k.flags & (sb::F_MASK_BITS | sb::F_MASK_U8)) off += 1264;
     k.sm_warp = (off + 127) / 128 * 128;
 }
 
