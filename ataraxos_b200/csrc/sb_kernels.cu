@@ -95,44 +95,83 @@ constexpr int ZERO_BYTES = 12800;  // MODE_STEP_PROD: per-CTA zero buffer, sourc
 // Legal moves
 // ---------------------------------------------------------------------------
 
-// Squares reachable from sq along `step` (at most maxs squares) for player p;
-// a scout slides until blocked, stopping on the first enemy
-// (csrc/stratego_buffer.cu:482-505).
-__device__ __forceinline__ int ray_len(const uint8_t* b, int sq, int step, int maxs, int p, bool scout) {
-    int len = 0;
-    for (int i = 0; i < maxs; ++i) {
-        sq += step;
-        if (is_lake(sq)) break;
-        const uint8_t c = b[sq];
-        if (c & C_OCC) {
-            if (((c >> 4) & 1) != p) ++len;
-            break;
-        }
-        ++len;
-        if (!scout) break;
-    }
-    return len;
+// Move generation on bitboards.  The 100 squares form two 128-bit boards
+// held in four registers each, row-major (square r*10+c) and column-major
+// (index c*10+r), built with ballots.  A piece's four rays are ffs / clz
+// searches on the 10-bit line of its row or column: stoppers S (own pieces
+// and lakes: neither entered nor passed) and enemies E (entered, end the
+// slide); non-scouts keep one square (csrc/stratego_buffer.cu:467-506).
+
+// Lakes: squares 42,43,46,47,52,53,56,57 (stratego/constants.py:25-28), and
+// their column-major indices 24,25,34,35,64,65,74,75.
+__device__ __forceinline__ uint32_t lake_word(int k) { return k == 1 ? 0x0330CC00u : 0u; }
+__device__ __forceinline__ uint32_t lake_word_t(int k) { return k == 0 ? 0x03000000u : (k == 1 ? 0x0000000Cu : (k == 2 ? 0x00000C03u : 0u)); }
+
+// The 10 bits of a 128-bit board (w0..w3) that start at bit pos (a multiple of 10).
+__device__ __forceinline__ uint32_t line10(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, int pos) {
+    const int i = pos >> 5;
+    const uint32_t lo = i == 0 ? w0 : (i == 1 ? w1 : (i == 2 ? w2 : w3));
+    const uint32_t hi = i == 0 ? w1 : (i == 1 ? w2 : (i == 2 ? w3 : 0u));
+    return __funnelshift_r(lo, hi, pos & 31) & 0x3FFu;
+}
+// Squares reachable from position x of a line towards higher positions ...
+__device__ __forceinline__ int ray_fwd(uint32_t S, uint32_t E, int x) {
+    const uint32_t m = ((S | E) >> (x + 1)) & ((1u << (9 - x)) - 1u);
+    if (!m) return 9 - x;
+    const int f = __ffs(m) - 1;
+    return f + (int)((E >> (x + 1 + f)) & 1u);
+}
+// ... and towards lower positions.
+__device__ __forceinline__ int ray_back(uint32_t S, uint32_t E, int x) {
+    const uint32_t m = (S | E) & ((1u << x) - 1u);
+    if (!m) return x;
+    const int h = 31 - __clz(m);
+    return (x - 1 - h) + (int)((E >> h) & 1u);
 }
 
 // Ray lengths of every lane square for side p, packed as up | left<<4 |
-// right<<8 | down<<12 (the groups in ascending destination order), and the
-// per-square counts (csrc/stratego_buffer.cu:467-506).
+// right<<8 | down<<12 (the groups in ascending destination order) into
+// rays[], and the per-square counts.
 __device__ __forceinline__ void enumerate(const uint8_t* b, int p, uint16_t* rays, int lane, int cnt[4]) {
+    uint32_t own[4], opp[4], ownT[4], oppT[4];
+    uint8_t code[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int i = lane + 32 * k;
+        const uint8_t c = i < NSQ ? b[i] : 0;
+        const uint8_t ct = i < NSQ ? b[(i % 10) * 10 + i / 10] : 0;
+        code[k] = c;
+        const bool co = c & C_OCC, cto = ct & C_OCC;
+        const bool cm = co && ((c >> 4) & 1) == p, ctm = cto && ((ct >> 4) & 1) == p;
+        own[k] = __ballot_sync(FULL, cm);
+        opp[k] = __ballot_sync(FULL, co && !cm);
+        ownT[k] = __ballot_sync(FULL, ctm);
+        oppT[k] = __ballot_sync(FULL, cto && !ctm);
+    }
+    const uint32_t S0 = own[0] | lake_word(0), S1 = own[1] | lake_word(1), S2 = own[2] | lake_word(2), S3 = own[3] | lake_word(3);
+    const uint32_t T0 = ownT[0] | lake_word_t(0), T1 = ownT[1] | lake_word_t(1), T2 = ownT[2] | lake_word_t(2),
+                   T3 = ownT[3] | lake_word_t(3);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int sq = lane + 32 * k;
         cnt[k] = 0;
         if (sq < NSQ) {
-            const uint8_t c = b[sq];
+            const uint8_t c = code[k];
             const int pc = c & C_PIECE;
             uint16_t packed = 0;
             if ((c & C_OCC) && ((c >> 4) & 1) == p && can_move(pc)) {
-                const bool scout = pc == 2;
-                const int r = sq / 10, col = sq % 10;
-                const int up = ray_len(b, sq, -10, r, p, scout);
-                const int left = ray_len(b, sq, -1, col, p, scout);
-                const int right = ray_len(b, sq, 1, 9 - col, p, scout);
-                const int down = ray_len(b, sq, 10, 9 - r, p, scout);
+                const int r = sq / 10, col = sq - 10 * r;
+                const uint32_t rs = line10(S0, S1, S2, S3, 10 * r), re = line10(opp[0], opp[1], opp[2], opp[3], 10 * r);
+                const uint32_t cs = line10(T0, T1, T2, T3, 10 * col);
+                const uint32_t ce = line10(oppT[0], oppT[1], oppT[2], oppT[3], 10 * col);
+                int up = ray_back(cs, ce, r), down = ray_fwd(cs, ce, r);
+                int left = ray_back(rs, re, col), right = ray_fwd(rs, re, col);
+                if (pc != 2) {
+                    up = min(up, 1);
+                    down = min(down, 1);
+                    left = min(left, 1);
+                    right = min(right, 1);
+                }
                 packed = (uint16_t)(up | (left << 4) | (right << 8) | (down << 12));
                 cnt[k] = up + left + right + down;
             }
@@ -155,28 +194,30 @@ __device__ __forceinline__ int decode_ray(int sq, uint32_t r, int j) {
 }
 
 // kth legal action in ascending src*100+dst order (warp-uniform result).
+// The four 32-square blocks are scanned together, two 16-bit sums per word.
 __device__ int kth_action(int kth, const int cnt[4], const uint16_t* rays, int lane) {
-    int base = 0;
+    uint32_t a01 = (uint32_t)cnt[0] | ((uint32_t)cnt[1] << 16), a23 = (uint32_t)cnt[2] | ((uint32_t)cnt[3] << 16);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int c = cnt[k];
-        int incl = c;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int v = __shfl_up_sync(FULL, incl, o);
-            if (lane >= o) incl += v;
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t v01 = __shfl_up_sync(FULL, a01, o), v23 = __shfl_up_sync(FULL, a23, o);
+        if (lane >= o) {
+            a01 += v01;
+            a23 += v23;
         }
-        const int total = __shfl_sync(FULL, incl, 31);
-        if (kth < base + total) {
-            const unsigned m = __ballot_sync(FULL, kth < base + incl);
-            const int L = __ffs(m) - 1;
-            const int excl = __shfl_sync(FULL, incl - c, L);
-            const int sq = L + 32 * k;
-            return sq * 100 + decode_ray(sq, rays[sq], kth - base - excl);
-        }
-        base += total;
     }
-    return -1;
+    const uint32_t t01 = __shfl_sync(FULL, a01, 31), t23 = __shfl_sync(FULL, a23, 31);
+    const int b1 = (int)(t01 & 0xFFFF), b2 = b1 + (int)(t01 >> 16), b3 = b2 + (int)(t23 & 0xFFFF);
+    const int k = kth < b1 ? 0 : (kth < b2 ? 1 : (kth < b3 ? 2 : 3));
+    const int base = k == 0 ? 0 : (k == 1 ? b1 : (k == 2 ? b2 : b3));
+    const uint32_t aw = k < 2 ? a01 : a23;
+    const int incl = (int)(k & 1 ? aw >> 16 : aw & 0xFFFF);
+    const int c = k == 0 ? cnt[0] : (k == 1 ? cnt[1] : (k == 2 ? cnt[2] : cnt[3]));
+    const unsigned m = __ballot_sync(FULL, kth < base + incl);
+    if (!m) return -1;
+    const int L = __ffs(m) - 1;
+    const int excl = __shfl_sync(FULL, incl - c, L);
+    const int sq = L + 32 * k;
+    return sq * 100 + decode_ray(sq, rays[sq], kth - base - excl);
 }
 
 __device__ __forceinline__ int count_of(const int cnt[4]) { return warp_sum(cnt[0] + cnt[1] + cnt[2] + cnt[3]); }
@@ -192,9 +233,10 @@ __device__ __forceinline__ void logit_noise(uint64_t seed, int64_t ge, int64_t p
 // Choose an action for the current state (rays/cnt already enumerated).
 // Uniform: k = (u32 * n) >> 32 over ascending legal actions.  Gumbel: argmax
 // of logit + Gumbel over legal actions, ties to the smaller action index.
+// u_pre: the uniform policy's Philox word when the caller drew it already.
 template <int POL>
 __device__ void choose(const KArgs& a, const uint16_t* rays, const int cnt[4], int n, int64_t e, int64_t ply,
-                       int lane, int& act, float& lp, int16_t* acts = nullptr) {
+                       int lane, int& act, float& lp, int16_t* acts = nullptr, const uint32_t* u_pre = nullptr) {
     const int64_t ge = a.env_base + e;
     if (n == 0) {
         act = -1;
@@ -203,8 +245,9 @@ __device__ void choose(const KArgs& a, const uint16_t* rays, const int cnt[4], i
     }
     const int pol = POL >= 0 ? POL : a.policy;
     if (pol == SB_POLICY_UNIFORM) {
-        const uint4 w = philox((uint32_t)ge, (uint32_t)ply, (uint32_t)((uint64_t)ply >> 32), TAG_ACTION, a.seed);
-        act = kth_action((int)mulshift(w.x, (uint32_t)n), cnt, rays, lane);
+        const uint32_t u =
+            u_pre ? *u_pre : philox((uint32_t)ge, (uint32_t)ply, (uint32_t)((uint64_t)ply >> 32), TAG_ACTION, a.seed).x;
+        act = kth_action((int)mulshift(u, (uint32_t)n), cnt, rays, lane);
         lp = -logf((float)n);
         return;
     }
@@ -884,6 +927,12 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
             const int64_t s_next = has(F_APPLY) ? (a.slot0 + p + 1) % a.n_slots : a.slot0 % a.n_slots;
             const int64_t ic = s_cur * a.n + e, in = s_next * a.n + e;
             uint8_t* ginfo = has(F_INFO) ? reinterpret_cast<uint8_t*>(a.info) + in * info_env : nullptr;
+            // the uniform proposal's random word depends only on (seed, env,
+            // ply): drawn first, off the game logic's critical path
+            const int64_t pp = has(F_PROPOSE) ? (has(F_APPLY) ? ply + 1 : ply) : a.ply;
+            uint32_t u_prop = 0;
+            if (kPol == SB_POLICY_UNIFORM)
+                u_prop = philox((uint32_t)(a.env_base + e), (uint32_t)pp, (uint32_t)((uint64_t)pp >> 32), TAG_ACTION, a.seed).x;
           if (live) {
             struct {
                 bool valid = false, term = false, ended = false;
@@ -975,10 +1024,9 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                 n = count_of(cnt);
             }
             if (has(F_PROPOSE) || has(F_SAMPLE_OUT)) {
-                const int64_t pp = has(F_PROPOSE) ? (has(F_APPLY) ? ply + 1 : ply) : a.ply;
                 int ac;
                 float lp;
-                choose<kPol>(a, rays, cnt, n, e, pp, lane, ac, lp, acts);
+                choose<kPol>(a, rays, cnt, n, e, pp, lane, ac, lp, acts, kPol == SB_POLICY_UNIFORM ? &u_prop : nullptr);
                 if (lane == 0) {
                     if (has(F_PROPOSE)) {
                         fld<int16_t>(rec, R_PROP) = (int16_t)ac;
