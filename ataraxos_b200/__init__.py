@@ -5,6 +5,6 @@ class and runs every method as hand-written sm_100a CUDA from
 ``_lib/libstratego_b200.so`` (C ABI: ``include/stratego_b200.h``).
 """
 
-from .buffer import StepOutput, StrategoRolloutBuffer, zobrist_table
+from .buffer import HostStepOutput, StepOutput, StrategoRolloutBuffer, zobrist_table
 
-__all__ = ["StrategoRolloutBuffer", "StepOutput", "zobrist_table"]
+__all__ = ["StrategoRolloutBuffer", "StepOutput", "HostStepOutput", "zobrist_table"]

@@ -92,6 +92,18 @@ class SbExport(ctypes.Structure):
     _fields_ = [(f, vp) for f in EXPORT_FIELDS]
 
 
+class SbHostIo(ctypes.Structure):
+    _fields_ = [
+        ("actions_host", vp),
+        ("actions_dev", vp),
+        ("back_dev", vp),
+        ("back_host", vp),
+        ("back_bytes", ctypes.c_int64),
+        ("sync", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+    ]
+
+
 # name -> (restype, argtypes)
 _SIGS = {
     "sb_abi_version": (ctypes.c_int, []),
@@ -104,6 +116,8 @@ _SIGS = {
     "sb_apply_actions": (ctypes.c_int, [ctypes.POINTER(SbState), vp, vp]),
     "sb_step": (ctypes.c_int, [ctypes.POINTER(SbState), vp, ctypes.c_int64, ctypes.POINTER(SbPolicy), ctypes.c_int,
                                ctypes.POINTER(SbStepOut), vp]),
+    "sb_step_host": (ctypes.c_int, [ctypes.POINTER(SbState), ctypes.POINTER(SbHostIo), ctypes.c_int64,
+                                    ctypes.POINTER(SbPolicy), ctypes.c_int, ctypes.POINTER(SbStepOut), vp]),
     "sb_rollout": (ctypes.c_int, [ctypes.POINTER(SbState), ctypes.c_int64, ctypes.POINTER(SbPolicy), ctypes.c_int,
                                   ctypes.c_int32, ctypes.POINTER(SbTraj), vp]),
     "sb_belief_resample": (ctypes.c_int, [ctypes.POINTER(SbState), ctypes.POINTER(SbState), vp, vp]),

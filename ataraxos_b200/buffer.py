@@ -65,6 +65,24 @@ def _stream(device: torch.device) -> ctypes.c_void_p:
 
 _POLICIES = {"uniform": C.SB_POLICY_UNIFORM, "gumbel": C.SB_POLICY_GUMBEL}
 
+_RESULT_FIELDS = (("reward", torch.float32, 4), ("next_action", torch.int16, 2), ("done", torch.uint8, 1))
+
+
+def _results_layout(n: int) -> dict[str, int]:
+    """Byte offsets of reward f32[n], next_action i16[n] and done u8[n] in one
+    block, each 16-byte aligned."""
+    lay, off = {}, 0
+    for name, _, size in _RESULT_FIELDS:
+        lay[name] = off
+        off += (n * size + 15) // 16 * 16
+    lay["bytes"] = max(off, 16)
+    return lay
+
+
+def _results_view(block: torch.Tensor, lay: dict[str, int], name: str, n: int) -> torch.Tensor:
+    dtype, size = {f: (d, s) for f, d, s in _RESULT_FIELDS}[name]
+    return block[lay[name]:lay[name] + n * size].view(dtype)
+
 
 @dataclass
 class StepOutput:
@@ -78,6 +96,17 @@ class StepOutput:
     logprob: torch.Tensor            # [N] float32, log-prob of the applied action when sampled
     next_action: torch.Tensor        # [N] int16, action proposed for the new state
     next_logprob: torch.Tensor       # [N] float32
+
+
+@dataclass
+class HostStepOutput:
+    """Pinned host copies of one step's per-game results, plus the step's
+    device outputs (all overwritten by the next ``step_host``)."""
+
+    reward: torch.Tensor       # [N] float32, player-0 reward of the transition
+    done: torch.Tensor         # [N] bool
+    next_action: torch.Tensor  # [N] int16, action proposed for the new state
+    device: StepOutput
 
 
 class StrategoRolloutBuffer:
@@ -138,6 +167,7 @@ class StrategoRolloutBuffer:
             C.call("sb_init_state", ctypes.byref(self._st), _stream(dev))
         self._ply = 0
         self._outs: dict[str, torch.Tensor] | None = None
+        self._host: dict | None = None
 
     # ------------------------------------------------------------------
     # plumbing
@@ -394,13 +424,18 @@ class StrategoRolloutBuffer:
         if self._outs is None:
             n, dev = self._n, self.device
             chans = NUM_CHANNELS if self.obs_layout == "dense" else COMPACT_CHANNELS
+            # reward, next_action and done share one block (see _results_layout) so
+            # that step_host brings all three back with a single copy.
+            lay = _results_layout(n)
+            res = torch.zeros(lay["bytes"], dtype=torch.uint8, device=dev)
             o: dict[str, torch.Tensor] = {
                 "infostate": torch.zeros((n, chans, 10, 10), dtype=self.obs_dtype, device=dev),
-                "reward": torch.zeros(n, dtype=torch.float32, device=dev),
-                "done": torch.zeros(n, dtype=torch.uint8, device=dev),
+                "results": res,
+                "reward": _results_view(res, lay, "reward", n),
+                "done": _results_view(res, lay, "done", n),
                 "action": torch.zeros(n, dtype=torch.int64, device=dev),
                 "logprob": torch.zeros(n, dtype=torch.float32, device=dev),
-                "next_action": torch.zeros(n, dtype=torch.int16, device=dev),
+                "next_action": _results_view(res, lay, "next_action", n),
                 "next_logprob": torch.zeros(n, dtype=torch.float32, device=dev),
                 "stats": torch.zeros(5, dtype=torch.int64, device=dev),
             }
@@ -460,9 +495,14 @@ class StrategoRolloutBuffer:
         outputs and are overwritten by the next step.
         """
         o = self._ensure_outputs()
+        self.step_raw(actions, policy=policy, logits=logits, auto_reset=auto_reset,
+                      outputs=self._step_out(o, observe))
+        return self._step_views(o, observe)
+
+    def _step_out(self, o: dict[str, torch.Tensor], observe: bool) -> C.SbStepOut:
         info = o["infostate"] if observe else None
         mask = o.get("mask") if observe else None
-        out = C.SbStepOut(
+        return C.SbStepOut(
             mask_u8=_vp(mask) if self.mask_format == "u8" else None,
             mask_bits=_vp(mask) if self.mask_format == "bits" else None,
             infostate=_vp(info),
@@ -477,12 +517,14 @@ class StrategoRolloutBuffer:
             hash=None,
             stats=o["stats"].data_ptr(),
         )
-        self.step_raw(actions, policy=policy, logits=logits, auto_reset=auto_reset, outputs=out)
+
+    def _step_views(self, o: dict[str, torch.Tensor], observe: bool) -> StepOutput:
+        mask = o.get("mask") if observe else None
         legal = None
         if mask is not None:
             legal = mask.view(torch.bool) if self.mask_format == "u8" else mask
         return StepOutput(
-            infostate=info,
+            infostate=o["infostate"] if observe else None,
             legal_mask=legal,
             reward=o["reward"],
             done=o["done"].view(torch.bool),
@@ -491,6 +533,73 @@ class StrategoRolloutBuffer:
             next_action=o["next_action"],
             next_logprob=o["next_logprob"],
         )
+
+    def step_host(
+        self,
+        actions: torch.Tensor | None = None,
+        *,
+        policy: str = "uniform",
+        auto_reset: bool = True,
+        observe: bool = True,
+        sync: bool = True,
+    ) -> HostStepOutput:
+        """``step`` for a host-side caller, in one native call: the (N,) int64
+        CPU ``actions`` (None: sample on the device) go host->device, the fused
+        ply runs, and reward / done / next_action come back into pinned host
+        memory with one copy.  The returned host tensors (and ``.device``, the
+        step's device outputs) are overwritten by the next call; with
+        ``sync=False`` they are valid once the current stream has reached this
+        call's end."""
+        h = self._host_io()
+        io = h["io"]
+        if actions is None:
+            io.actions_host = None
+        else:
+            if not isinstance(actions, torch.Tensor) or actions.device.type != "cpu":
+                raise RuntimeError("step_host takes CPU actions (use step() for device tensors)")
+            if actions.dim() != 1 or actions.size(0) != self._n or actions.dtype != torch.int64:
+                raise RuntimeError(f"actions must be int64 ({self._n},)")
+            if not (actions.is_contiguous() and actions.is_pinned()):
+                h["act"].copy_(actions)
+                actions = h["act"]
+            io.actions_host = actions.data_ptr()
+        io.sync = int(sync)
+        pol = h["pol"].get(policy)
+        if pol is None:
+            pol = h["pol"][policy] = self._policy(policy, None)
+        out = h["out"][bool(observe)]
+        if torch.cuda.current_device() != self._device_id:
+            with torch.cuda.device(self.device):
+                C.call("sb_step_host", ctypes.byref(self._st), ctypes.byref(io), self._ply, ctypes.byref(pol),
+                       int(auto_reset), ctypes.byref(out), _stream(self.device))
+        else:
+            C.call("sb_step_host", ctypes.byref(self._st), ctypes.byref(io), self._ply, ctypes.byref(pol),
+                   int(auto_reset), ctypes.byref(out), _stream(self.device))
+        self._ply += 1
+        return h["ret"][bool(observe)]
+
+    def _host_io(self) -> dict:
+        if self._host is None:
+            o = self._ensure_outputs()
+            n, lay = self._n, _results_layout(self._n)
+            back = torch.zeros(lay["bytes"], dtype=torch.uint8, pin_memory=True)
+            outs, rets = {}, {}
+            for observe in (False, True):
+                outs[observe] = self._step_out(o, observe)
+                rets[observe] = HostStepOutput(
+                    reward=_results_view(back, lay, "reward", n),
+                    done=_results_view(back, lay, "done", n).view(torch.bool),
+                    next_action=_results_view(back, lay, "next_action", n),
+                    device=self._step_views(o, observe),
+                )
+            d_act = self._alloc((max(n, 1),), torch.int64)
+            self._host = {
+                "back": back, "d_act": d_act, "out": outs, "ret": rets, "pol": {},
+                "act": torch.zeros(max(n, 1), dtype=torch.int64, pin_memory=True)[:n],
+                "io": C.SbHostIo(actions_host=None, actions_dev=d_act.data_ptr(), back_dev=o["results"].data_ptr(),
+                                 back_host=back.data_ptr(), back_bytes=lay["bytes"], sync=1, reserved=0),
+            }
+        return self._host
 
     def episode_stats(self) -> torch.Tensor:
         """int64 [5]: games finished in step(), red wins, blue wins, draws, Σ lengths."""

@@ -1616,6 +1616,34 @@ int sb_step(const sb_state* s, const int64_t* actions, int64_t ply, const sb_pol
     return launch_env(k, dtype, (cudaStream_t)stream);
 }
 
+int sb_step_host(const sb_state* s, const sb_host_io* io, int64_t ply, const sb_policy* policy, int auto_reset,
+                 const sb_step_out* out, void* stream) {
+    int rc = check_state(s);
+    if (rc != SB_OK) return rc;
+    if (!io) return fail(SB_E_ARG, "io is NULL");
+    if (io->actions_host && !io->actions_dev) return fail(SB_E_ARG, "actions_host needs actions_dev");
+    if (io->back_bytes < 0 || (io->back_bytes > 0 && (!io->back_dev || !io->back_host)))
+        return fail(SB_E_ARG, "bad copy-back range");
+    cudaStream_t st = (cudaStream_t)stream;
+    if (io->actions_host && s->n > 0) {
+        cudaError_t e = cudaMemcpyAsync(io->actions_dev, io->actions_host, (size_t)s->n * sizeof(int64_t),
+                                        cudaMemcpyHostToDevice, st);
+        if (e != cudaSuccess) return cuda_fail(e, "actions host->device");
+    }
+    rc = sb_step(s, io->actions_host ? io->actions_dev : nullptr, ply, policy, auto_reset, out, stream);
+    if (rc != SB_OK) return rc;
+    if (io->back_bytes > 0) {
+        cudaError_t e = cudaMemcpyAsync(io->back_host, io->back_dev, (size_t)io->back_bytes,
+                                        cudaMemcpyDeviceToHost, st);
+        if (e != cudaSuccess) return cuda_fail(e, "results device->host");
+    }
+    if (io->sync) {
+        cudaError_t e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) return cuda_fail(e, "stream synchronize");
+    }
+    return SB_OK;
+}
+
 int sb_rollout(const sb_state* s, int64_t ply, const sb_policy* policy, int auto_reset, int32_t n_plies,
                const sb_traj* traj, void* stream) {
     int rc = check_state(s);

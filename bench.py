@@ -272,33 +272,27 @@ def timed_launches(ctx: Ctx, launch, k: int, flush_mib: int):
 
 
 def e2e_loop(ctx: Ctx, buf, steps: int, policy: str = "uniform") -> tuple[float, int, int]:
-    """The public API with host buffers: per step the actions (int64[B]) go
-    host->device from pinned memory, the fused step runs, and reward, done and
-    the next proposed actions come back into pinned memory (the host takes
-    the proposals as its next actions).  Returns (updates/s, h2d, d2h bytes)."""
+    """The public host-side API, ``StrategoRolloutBuffer.step_host``: per step the
+    actions (int64[B], pinned host memory) go host->device, the fused step runs,
+    and reward, done and the next proposed actions come back into pinned host
+    memory with one copy; the call returns once they have landed.  The host
+    takes the proposals as its next actions.  Returns (updates/s, h2d, d2h bytes)."""
     B = buf.n_games
     h_act = torch.empty(B, dtype=torch.int64, pin_memory=True)
-    h_rew = torch.empty(B, dtype=torch.float32, pin_memory=True)
-    h_done = torch.empty(B, dtype=torch.uint8, pin_memory=True)
-    h_next = torch.empty(B, dtype=torch.int16, pin_memory=True)
-    out = buf.step(None, policy=policy)
-    h_next.copy_(out.next_action)
+    r = buf.step_host(None, policy=policy)
     ctx.barrier()
     torch.cuda.synchronize(ctx.dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(ctx.stream)
     for _ in range(steps):
-        h_act.copy_(h_next)
-        out = buf.step(h_act, policy=policy)
-        h_rew.copy_(out.reward, non_blocking=True)
-        h_done.copy_(out.done.view(torch.uint8), non_blocking=True)
-        h_next.copy_(out.next_action, non_blocking=True)
-        ctx.stream.synchronize()
+        h_act.copy_(r.next_action)
+        r = buf.step_host(h_act, policy=policy)
     e1.record(ctx.stream)
     torch.cuda.synchronize(ctx.dev)
     ctx.barrier()
     ms = ctx.max_over_ranks(e0.elapsed_time(e1))
-    return ctx.world * B * steps / (ms / 1e3), B * 8, B * (4 + 1 + 2)
+    return ctx.world * B * steps / (ms / 1e3), B * 8, int(r.reward.numel() * 4 + r.next_action.numel() * 2
+                                                            + r.done.numel())
 
 
 def run_step_config(ctx: Ctx, cfg: int) -> dict:

@@ -237,6 +237,42 @@ def test_host_actions_step_equals_reference_api():
     assert_state_equal(export_np(a), export_np(c), "step vs apply_actions")
 
 
+@pytest.mark.parametrize("pinned", [True, False])
+def test_step_host_equals_step(pinned):
+    """sb_step_host (host actions in, reward/done/next_action back into pinned
+    memory in one call) drives the game exactly as step() with device tensors,
+    for host-chosen actions (the previous proposals) and device sampling."""
+    n = 300
+    pool = torch.from_numpy(oracle.make_setup_pool(17, 512))
+    h = _buf(n, seed=17, setup_pool=pool, no_attack_limit=30)
+    d = _buf(n, seed=17, setup_pool=pool, no_attack_limit=30)
+    h.reset_all_from_pool()
+    d.reset_all_from_pool()
+    r = h.step_host(None)
+    ref = d.step(None)
+    for t in range(80):
+        np.testing.assert_array_equal(r.next_action.numpy(), ref.next_action.cpu().numpy(), err_msg=f"ply {t}")
+        np.testing.assert_array_equal(r.reward.numpy(), ref.reward.cpu().numpy())
+        np.testing.assert_array_equal(r.done.numpy(), ref.done.cpu().numpy())
+        if t % 3 == 2:
+            r, ref = h.step_host(None), d.step(None)
+            continue
+        acts = r.next_action.to(torch.int64)
+        if pinned:
+            acts = acts.pin_memory()
+        if t % 5 == 0:
+            acts[::7] = 0  # illegal: ignored and counted for those games
+        r = h.step_host(acts)
+        ref = d.step(acts.to("cuda"))
+        assert torch.equal(r.device.infostate, ref.infostate)
+        assert torch.equal(r.device.legal_mask, ref.legal_mask)
+    assert_state_equal(export_np(h), export_np(d), "step_host vs step")
+    with pytest.raises(RuntimeError):
+        h.step_host(torch.zeros(n, dtype=torch.int64, device="cuda"))
+    with pytest.raises(RuntimeError):
+        h.step_host(torch.zeros(n - 1, dtype=torch.int64))
+
+
 def test_shard_invariance_env_base():
     """A buffer owning envs [64,128) reproduces those envs of a 128-env buffer."""
     pool = oracle.make_setup_pool(21, 1024)
