@@ -42,6 +42,8 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+from ataraxos_b200 import sharding  # noqa: E402
+
 SEED = 20251107
 POOL = 65536
 FALLBACK_HBM_GBS = 6650.0
@@ -163,7 +165,7 @@ def run_reference(args, rank: int) -> None:
     import oracle
 
     threads = os.cpu_count() or 1
-    envs = min(args.envs, 64 * threads)
+    envs = args.envs  # the config-2 batch itself; one step is one ply of every game
     pool = oracle.make_setup_pool(SEED, 4096)
     o = oracle.OracleState(envs, seed=SEED, pool=pool)
     o.reset_pool(force_all=True)
@@ -231,18 +233,11 @@ class Ctx:
             self.dist.barrier()
 
     def max_over_ranks(self, v: float) -> float:
-        t = torch.tensor([v], dtype=torch.float64, device=self.dev)
-        if self.world > 1:
-            self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
-        return float(t.item())
+        return sharding.max_over_ranks(v, self.dev)
 
     def gather_stats(self, stats: torch.Tensor) -> list[int]:
         """End-of-rollout NCCL all-gather of each rank's int64[5] episode statistics."""
-        if self.world > 1:
-            g = torch.empty((self.world, 5), dtype=torch.int64, device=self.dev)
-            self.dist.all_gather_into_tensor(g, stats.contiguous())
-            return g.sum(0).tolist()
-        return stats.tolist()
+        return sharding.gather_episode_stats(stats).sum(0).tolist()
 
 
 def timed_launches(ctx: Ctx, launch, k: int, flush_mib: int):
@@ -271,7 +266,8 @@ def timed_launches(ctx: Ctx, launch, k: int, flush_mib: int):
     return total_ms, clocks.summary()
 
 
-def e2e_loop(ctx: Ctx, buf, steps: int, policy: str = "uniform") -> tuple[float, int, int]:
+def e2e_loop(ctx: Ctx, buf, steps: int, policy: str = "uniform", total_envs: int | None = None
+             ) -> tuple[float, int, int]:
     """The public host-side API, ``StrategoRolloutBuffer.step_host``: per step the
     actions (int64[B], pinned host memory) go host->device, the fused step runs,
     and reward, done and the next proposed actions come back into pinned host
@@ -291,7 +287,8 @@ def e2e_loop(ctx: Ctx, buf, steps: int, policy: str = "uniform") -> tuple[float,
     torch.cuda.synchronize(ctx.dev)
     ctx.barrier()
     ms = ctx.max_over_ranks(e0.elapsed_time(e1))
-    return ctx.world * B * steps / (ms / 1e3), B * 8, int(r.reward.numel() * 4 + r.next_action.numel() * 2
+    total = ctx.world * B if total_envs is None else total_envs
+    return total * steps / (ms / 1e3), B * 8, int(r.reward.numel() * 4 + r.next_action.numel() * 2
                                                             + r.done.numel())
 
 
@@ -305,8 +302,8 @@ def run_step_config(ctx: Ctx, cfg: int) -> dict:
         B, pool, policy, env_base = a.envs, POOL, "uniform", ctx.rank * a.envs
     else:
         total = a.envs if a.envs != 4096 else 262144
-        B, pool, policy = total // ctx.world, 1 << 20, "gumbel"
-        env_base = ctx.rank * B
+        env_base, B = sharding.shard_range(total, ctx.world, ctx.rank)
+        pool, policy = 1 << 20, "gumbel"
     buf = StrategoRolloutBuffer(B, ctx.local, seed=SEED, env_base=env_base, pool_size=pool, pool_seed=SEED,
                                 obs_dtype=torch.bfloat16, obs_layout="dense", mask_format="u8")
     buf.reset_all_from_pool()
@@ -324,14 +321,15 @@ def run_step_config(ctx: Ctx, cfg: int) -> dict:
         l2 = f"flushed between timed steps ({a.flush_mib} MiB write, then {a.flush_mib // 2} MiB read)"
         scaling = "weak"
     else:
-        e2e, h2d, d2h = e2e_loop(ctx, buf, max(10, a.e2e_steps // 10), policy)
-        workload = (f"config3: {B * ctx.world} envs split over {ctx.world} GPU(s) ({B}/GPU), actions by Gumbel-max "
+        e2e, h2d, d2h = e2e_loop(ctx, buf, max(10, a.e2e_steps // 10), policy, total)
+        workload = (f"config3: {total} envs split over {ctx.world} GPU(s) ({B}/GPU), actions by Gumbel-max "
                     "over virtual Philox N(0,1) logits of the legal moves (logits never materialised), setups from "
                     f"a {pool}-entry pool, auto-reset, bf16 dense infostate + u8 mask")
         l2 = "outputs of one step (25.5 KB/env) exceed L2 many times; no flush"
         scaling = "strong"
     return {
-        "value": ctx.world * B * a.steps / (total_ms / 1e3), "ms_per_step": launch_ms, "launch_ms": launch_ms,
+        "value": (ctx.world * B if cfg == 2 else total) * a.steps / (total_ms / 1e3), "ms_per_step": launch_ms,
+        "launch_ms": launch_ms,
         "envs_per_launch": B, "plies_per_launch": 1, "bytes_per_update": BYTES_PER_UPDATE, "clocks": clocks,
         "stats": stats, "e2e": {"value": e2e, "unit": "updates/s", "h2d_bytes_per_step": h2d,
                                 "d2h_bytes_per_step": d2h},
