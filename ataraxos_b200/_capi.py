@@ -16,6 +16,7 @@ SB_DTYPE_F32, SB_DTYPE_BF16 = 0, 1
 SB_LAYOUT_DENSE_ALL, SB_LAYOUT_DENSE_LIVE, SB_LAYOUT_COMPACT = 0, 1, 2
 SB_POLICY_UNIFORM, SB_POLICY_GUMBEL = 0, 1
 SB_STATUS_BAD_SETUP = 1
+SB_STATUS_WAIT_TIMEOUT = 2
 RECORD_BYTES = 256
 
 vp = ctypes.c_void_p

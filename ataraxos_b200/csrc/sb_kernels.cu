@@ -132,7 +132,9 @@ __device__ __forceinline__ int ray_back(uint32_t S, uint32_t E, int x) {
 // Ray lengths of every lane square for side p, packed as up | left<<4 |
 // right<<8 | down<<12 (the groups in ascending destination order) into
 // rays[], and the per-square counts.
-__device__ __forceinline__ void enumerate(const uint8_t* b, int p, uint16_t* rays, int lane, int cnt[4]) {
+// Not inlined: its three call sites share one copy of the code, which keeps
+// the step kernel's instruction footprint small.
+__device__ __noinline__ void enumerate(const uint8_t* b, int p, uint16_t* rays, int lane, int cnt[4]) {
     uint32_t own[4], opp[4], ownT[4], oppT[4];
     uint8_t code[4];
 #pragma unroll
@@ -693,16 +695,16 @@ __device__ void write_info_dense(const uint8_t* rec, const KArgs& a, int lane, u
     uint8_t* gl = g + lane * 4 * (int)sizeof(T);
     // 12-23: opponent, 1/12 where hidden, one-hot where revealed
     const typename Q::V hid_o = Q::sel(__vcmpne4(f.fl & 0x02020202u, 0u), TW);
-#pragma unroll
+#pragma unroll 1
     for (int t = 0; t < 12; ++t)
         Q::st(gl + (12 + t) * PB, Q::orv(Q::sel(__vcmpeq4(f.ort, (uint32_t)(t + 1) * 0x01010101u), ONE), hid_o));
     // 24-35: own pieces as the opponent sees them
     const typename Q::V hid_w = Q::sel(__vcmpne4(f.fl & 0x01010101u, 0u), TW);
-#pragma unroll
+#pragma unroll 1
     for (int t = 0; t < 12; ++t)
         Q::st(gl + (24 + t) * PB, Q::orv(Q::sel(__vcmpeq4(f.owt, (uint32_t)(t + 1) * 0x01010101u), ONE), hid_w));
     // 36 own hidden, 37 opponent hidden, 38 empty (lakes included), 39 own moved, 40 opponent moved
-#pragma unroll
+#pragma unroll 1
     for (int i = 0; i < 5; ++i) Q::st(gl + (36 + i) * PB, Q::sel(__vcmpne4(f.fl & ((1u << i) * 0x01010101u), 0u), ONE));
     // 41 / 42: the two fractions (exact float32 quotients)
     const int mn = fld<int32_t>(rec, R_MOVENUM), msa = fld<int32_t>(rec, R_MSA);
@@ -766,18 +768,15 @@ __device__ void bulk_zero_rows(const uint8_t* zb, uint8_t* gmask, uint8_t* ginfo
 
 // u8 legal-mask ones on top of a zeroed row (MODE_STEP_PROD).
 __device__ void mask_scatter(const uint16_t* rays, int lane, uint8_t* m) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int sq = lane + 32 * k;
-        if (sq >= NSQ) continue;
+    // rolled loops: every lane walks a different number of moves, and the
+    // unrolled form would multiply the code the warps fetch
+#pragma unroll 1
+    for (int sq = lane; sq < NSQ; sq += 32) {
         const uint32_t r = rays[sq];
-        if (!r) continue;
+        const int n = (r & 15) + ((r >> 4) & 15) + ((r >> 8) & 15) + (r >> 12);
         uint8_t* row = m + sq * 100;
-        const int up = r & 15, left = (r >> 4) & 15, right = (r >> 8) & 15, down = r >> 12;
-        for (int j = 1; j <= up; ++j) row[sq - 10 * j] = 1;
-        for (int j = 1; j <= left; ++j) row[sq - j] = 1;
-        for (int j = 1; j <= right; ++j) row[sq + j] = 1;
-        for (int j = 1; j <= down; ++j) row[sq + 10 * j] = 1;
+#pragma unroll 1
+        for (int j = 0; j < n; ++j) row[decode_ray(sq, r, j)] = 1;
     }
 }
 
@@ -853,20 +852,42 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
     };
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(16) int64_t s_zob[ZOB_N];
+    // s_bar[0]: the Zobrist table has landed.  MODE_STEP_PROD only: [1] the
+    // producer's zero rows of a batch are complete, [2] every env warp has
+    // seen [1] for that batch (the producer then starts the next batch).
+    __shared__ __align__(8) uint64_t s_bar[3];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     constexpr int ENVW = kProd ? WARPS - 1 : WARPS;  // warps that play envs
     const bool producer = kProd && w == WARPS - 1;
     uint8_t* zb = smem;  // MODE_STEP_PROD: the zero buffer precedes the warps' regions
     uint8_t* ws = smem + (kProd ? ZERO_BYTES : 0) + w * a.sm_warp;
-    // the Zobrist table lives in shared memory: the game logic never waits on
-    // HBM for it while the outputs stream out
-    for (int i = threadIdx.x; i < ZOB_N / 2; i += blockDim.x)
-        reinterpret_cast<uint4*>(s_zob)[i] = reinterpret_cast<const uint4*>(a.zob)[i];
-    if (kProd) {
-        for (int i = threadIdx.x; i < ZERO_BYTES / 16; i += blockDim.x) st16(zb + i * 16, make_uint4(0, 0, 0, 0));
-        fence_async_smem();
+    if (threadIdx.x == 0) {
+        mbar_init(&s_bar[0], 1);
+        mbar_init(&s_bar[1], 1);
+        mbar_init(&s_bar[2], ENVW);
+        mbar_fence_init();
     }
     __syncthreads();
+    // The Zobrist table lives in shared memory, so the game logic never waits
+    // on HBM for it while the outputs stream out.  One bulk copy brings it in
+    // while the warps load their records; a warp waits for it only before
+    // its first lookup.
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(&s_bar[0], ZOB_N * 8);
+        bulk_g2s(s_zob, a.zob, ZOB_N * 8, &s_bar[0]);
+    }
+    bool zob_ready = false;
+    auto zob_wait = [&]() {
+        if (!zob_ready) {
+            if (!mbar_wait(&s_bar[0], 0) && lane == 0 && a.status) atomicOr(a.status, SB_STATUS_WAIT_TIMEOUT);
+            zob_ready = true;
+        }
+    };
+    if (producer) {
+        for (int i = lane; i < ZERO_BYTES / 16; i += 32) st16(zb + i * 16, make_uint4(0, 0, 0, 0));
+        fence_async_smem();
+        __syncwarp();
+    }
     uint8_t* rec = ws;
     uint16_t* rays = reinterpret_cast<uint16_t*>(ws + SM_RAYS);
     int16_t* acts = reinterpret_cast<int16_t*>(ws + SM_ACTS);
@@ -875,21 +896,20 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
     const bool compact = a.info_layout == SB_LAYOUT_COMPACT;
     const int64_t info_env = (int64_t)(compact ? 76 : NCH) * PB;
     const int hist_off = (compact ? 44 : 456) * PB;
-    const int np = (kStep && a.n_plies > 1) ? a.n_plies : 1;
+    // MODE_STEP_PROD is single-ply: one batch of envs per iteration
+    const int np = (kStep && !kProd && a.n_plies > 1) ? a.n_plies : 1;
     const bool zeros = kProd && (has(F_INFO) || has(F_MASK_U8));
     const int64_t stride = (int64_t)gridDim.x * ENVW;
     const int64_t first = (int64_t)blockIdx.x * ENVW;
-    const int64_t last_iter = (first < a.n ? (a.n - first + stride - 1) / stride : 0) * np - 1;
     int64_t iter = 0;
     for (int64_t base = first; base < a.n; base += stride) {
         if (producer) {
-            for (int p = 0; p < np; ++p, ++iter) {
-                if (!zeros) continue;
-                if (iter > 0) named_sync(2, WARPS * 32);
+            if (zeros) {
+                // at most one batch ahead of the slowest env warp
+                if (iter > 0 && !mbar_wait(&s_bar[2], (uint32_t)((iter - 1) & 1)) && lane == 0 && a.status)
+                    atomicOr(a.status, SB_STATUS_WAIT_TIMEOUT);
                 if (lane == 0) {
-                    // the env warps' stores of the previous batch come first
-                    fence_async_global();
-                    const int64_t s_next = has(F_APPLY) ? (a.slot0 + p + 1) % a.n_slots : a.slot0 % a.n_slots;
+                    const int64_t s_next = has(F_APPLY) ? (a.slot0 + 1) % a.n_slots : a.slot0 % a.n_slots;
                     for (int j = 0; j < ENVW && base + j < a.n; ++j) {
                         const int64_t in = s_next * a.n + base + j;
                         bulk_zero_rows<T>(zb, has(F_MASK_U8) ? a.mask_u8 + in * NACT : nullptr,
@@ -898,11 +918,13 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                     }
                     bulk_commit();
                     bulk_wait_all();
+                    // the zero rows are written before anything stored on top
                     fence_async_global();
+                    mbar_arrive(&s_bar[1]);
                 }
                 __syncwarp();
-                named_arrive(1, WARPS * 32);
             }
+            ++iter;
             continue;
         }
         const int64_t e = base + w;
@@ -917,6 +939,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
         int cnt[4] = {0, 0, 0, 0};
 
         if (live && (has(F_RESET_PLANES) || has(F_RESET_POOL)) && (has(F_FORCE) || rec[R_TERM])) {
+            zob_wait();
             reset_env(rec, ring2, a, s_zob, e, has(F_RESET_POOL), lane);
             dirty = true;
         }
@@ -979,6 +1002,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                         __syncwarp();
                     } else {
                         bool chk, flag;
+                        zob_wait();
                         const bool ok = apply_env(rec, ring2, a, s_zob, act, lane, chk, flag);
                         if (ok) rays_ok = false;  // the board changed
                         if (!ok) {
@@ -1011,6 +1035,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                 __syncwarp();
                 dirty = true;
                 if (has(F_AUTO_RESET) && term) {
+                    zob_wait();
                     reset_env(rec, ring2, a, s_zob, e, true, lane);
                     rays_ok = false;
                 }
@@ -1061,11 +1086,19 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                 }
             }
             __syncwarp();
-            // outputs of the new state: dense rows first (no zero pass needed)
-            if (has(F_INFO)) write_info_dense<T>(rec, a, lane, ginfo);
+            // outputs of the new state.  Dense rows need no zero pass.  In
+            // MODE_STEP_PROD the odd warps write them last, so that their
+            // bandwidth-bound stream overlaps the even warps' scattered stores
+            // (request-bound) and the other way round.
+            if (has(F_INFO) && !(zeros && (w & 1))) write_info_dense<T>(rec, a, lane, ginfo);
           }
-            // MODE_STEP_PROD: this batch's zero rows are complete (producer)
-            if (zeros) named_sync(1, WARPS * 32);
+            if (zeros) {
+                // this batch's zero rows are complete (producer)
+                if (!mbar_wait(&s_bar[1], (uint32_t)(iter & 1)) && lane == 0 && a.status)
+                    atomicOr(a.status, SB_STATUS_WAIT_TIMEOUT);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_bar[2]);
+            }
           if (live) {
             const bool all = a.info_layout == SB_LAYOUT_DENSE_ALL;
             if (kProd) {
@@ -1083,14 +1116,16 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                     if (has(F_MASK_BITS)) write_mask_bits(wbits, lane, a.mask_bits + in * SB_MASK_BITS_BYTES);
                 }
             }
+            if (zeros && (w & 1) && has(F_INFO)) write_info_dense<T>(rec, a, lane, ginfo);
             __syncwarp();
           }
-            if (zeros && iter < last_iter) named_arrive(2, WARPS * 32);
         }
 
         if (live && dirty) reinterpret_cast<uint2*>(a.rec + e * REC)[lane] = reinterpret_cast<const uint2*>(rec)[lane];
         __syncwarp();
     }
+    // the table's bulk copy must land before the CTA's shared memory goes away
+    if (threadIdx.x == 0) zob_wait();
 }
 
 // ---------------------------------------------------------------------------
@@ -1345,7 +1380,8 @@ int check_state(const sb_state* s) {
     if (s->n < 0) return fail(SB_E_ARG, "n < 0");
     if (s->n == 0) return SB_OK;
     if (!s->records || !s->chase_ring || !s->zobrist) return fail(SB_E_ARG, "records/chase_ring/zobrist is NULL");
-    if (!aligned(s->records, 16) || !aligned(s->chase_ring, 16)) return fail(SB_E_ARG, "records/chase_ring not 16-byte aligned");
+    if (!aligned(s->records, 16) || !aligned(s->chase_ring, 16) || !aligned(s->zobrist, 16))
+        return fail(SB_E_ARG, "records/chase_ring/zobrist not 16-byte aligned");
     if (s->setup_pool && s->pool_size <= 0) return fail(SB_E_ARG, "setup_pool given with pool_size <= 0");
     if (s->pool_size > 0xFFFFFFFFll) return fail(SB_E_ARG, "pool_size above 2^32");
     return SB_OK;

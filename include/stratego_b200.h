@@ -77,6 +77,7 @@ typedef struct sb_state {
 } sb_state;
 
 #define SB_STATUS_BAD_SETUP 1   /* a setup plane or pool entry held a piece code > 12 */
+#define SB_STATUS_WAIT_TIMEOUT 2 /* a kernel gave up waiting (about 1 s) on an in-CTA handshake */
 
 /* Outputs of one fused step; any pointer may be NULL (not produced). */
 typedef struct sb_step_out {
