@@ -1,14 +1,14 @@
 """Trajectory ring and search rollouts on top of StrategoRolloutBuffer.
 
 ``TrajectoryBuffer`` is the self-play ring of the north-star contract
-T slots x N envs, each slot holding the observation
+(benchmark config 4): T slots x N envs, each slot holding the observation
 (bf16 infostate, compact 76-plane layout by default), the bit-packed legal
 mask, the sampled action (int16 src*100+dst), its log-prob, and the reward /
 done of the transition taken from that slot.  ``rollout(k)`` runs k plies in
 ONE kernel launch per call: every env's record stays on chip while the ply
 loop writes straight into the ring.
 
-``BeliefRollouts`` is the search batch: each root is
+``BeliefRollouts`` is the search batch (benchmark config 5): each root is
 copied into ``samples_per_root`` envs whose opponent identities are re-dealt
 consistently with the side to move's information, then every sample plays
 ``depth`` plies; per-ply legal masks and the terminal values come back.

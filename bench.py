@@ -5,7 +5,7 @@ uniform legal action, apply it with combat / trackers / terminal check,
 auto-reset from the seeded setup pool, emit the uint8 legal mask and the
 bfloat16 [488,10,10] infostate of the new state).
 
-Default workload = BASELINE config 2: 4096 envs per GPU, seeded random setups
+Default workload = benchmark config 2: 4096 envs per GPU, seeded random setups
 (pool of 65536), uniform random legal actions, auto-reset, bf16 infostate
 [B,488,10,10] (channels 43-455 are zero planes written once at allocation;
 every ply rewrites the 75 live channels), uint8 mask [B,100,100].  One step =
