@@ -63,6 +63,16 @@ def _stream(device: torch.device) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
+_get_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _raw_stream(index: int) -> int:
+    """cudaStream_t of the current torch stream of device ``index`` (as an int)."""
+    if _get_raw_stream is not None:
+        return _get_raw_stream(index)
+    return torch.cuda.current_stream(index).cuda_stream
+
+
 _POLICIES = {"uniform": C.SB_POLICY_UNIFORM, "gumbel": C.SB_POLICY_GUMBEL}
 
 _RESULT_FIELDS = (("reward", torch.float32, 4), ("next_action", torch.int16, 2), ("done", torch.uint8, 1))
@@ -542,6 +552,7 @@ class StrategoRolloutBuffer:
         auto_reset: bool = True,
         observe: bool = True,
         sync: bool = True,
+        mapped: bool = True,
     ) -> HostStepOutput:
         """``step`` for a host-side caller, in one native call: the (N,) int64
         CPU ``actions`` (None: sample on the device) go host->device, the fused
@@ -549,55 +560,83 @@ class StrategoRolloutBuffer:
         memory with one copy.  The returned host tensors (and ``.device``, the
         step's device outputs) are overwritten by the next call; with
         ``sync=False`` they are valid once the current stream has reached this
-        call's end."""
+        call's end.
+
+        ``mapped=True`` moves the data without copy-engine transfers: the
+        kernel reads the actions from page-locked host memory and writes
+        reward / done / next_action straight into the pinned result block
+        (the device copies of those three are then not written).
+        ``mapped=False`` copies actions in and the result block back with
+        ``cudaMemcpyAsync``."""
         h = self._host_io()
-        io = h["io"]
+        mode = "mapped" if mapped else "copy"
+        io = h["io"][mode]
         if actions is None:
             io.actions_host = None
         else:
-            if not isinstance(actions, torch.Tensor) or actions.device.type != "cpu":
+            if type(actions) is not torch.Tensor or actions.device.type != "cpu":
                 raise RuntimeError("step_host takes CPU actions (use step() for device tensors)")
-            if actions.dim() != 1 or actions.size(0) != self._n or actions.dtype != torch.int64:
+            if actions.shape != h["shape"] or actions.dtype is not torch.int64:
                 raise RuntimeError(f"actions must be int64 ({self._n},)")
-            if not (actions.is_contiguous() and actions.is_pinned()):
-                h["act"].copy_(actions)
-                actions = h["act"]
-            io.actions_host = actions.data_ptr()
-        io.sync = int(sync)
+            ptr = actions.data_ptr()
+            if ptr != h["pinned_ptr"]:  # pinned-ness checked once per buffer address
+                if not (actions.is_contiguous() and actions.is_pinned()):
+                    h["act"].copy_(actions)
+                    ptr = h["act"].data_ptr()
+                else:
+                    h["pinned_ptr"] = ptr
+            io.actions_host = ptr
+        io.sync = 1 if sync else 0
         pol = h["pol"].get(policy)
         if pol is None:
-            pol = h["pol"][policy] = self._policy(policy, None)
-        out = h["out"][bool(observe)]
-        if torch.cuda.current_device() != self._device_id:
+            pol = h["pol"][policy] = ctypes.byref(self._policy(policy, None))
+        dev = self._device_id
+        if torch.cuda.current_device() != dev:
             with torch.cuda.device(self.device):
-                C.call("sb_step_host", ctypes.byref(self._st), ctypes.byref(io), self._ply, ctypes.byref(pol),
-                       int(auto_reset), ctypes.byref(out), _stream(self.device))
+                rc = h["fn"](h["st"], h["bio"][mode], self._ply, pol, 1 if auto_reset else 0,
+                             h["out"][mode][bool(observe)], _raw_stream(dev))
         else:
-            C.call("sb_step_host", ctypes.byref(self._st), ctypes.byref(io), self._ply, ctypes.byref(pol),
-                   int(auto_reset), ctypes.byref(out), _stream(self.device))
+            rc = h["fn"](h["st"], h["bio"][mode], self._ply, pol, 1 if auto_reset else 0,
+                         h["out"][mode][bool(observe)], _raw_stream(dev))
+        if rc:
+            C.check(rc)
         self._ply += 1
-        return h["ret"][bool(observe)]
+        return h["ret"][mode][bool(observe)]
 
     def _host_io(self) -> dict:
         if self._host is None:
             o = self._ensure_outputs()
             n, lay = self._n, _results_layout(self._n)
             back = torch.zeros(lay["bytes"], dtype=torch.uint8, pin_memory=True)
-            outs, rets = {}, {}
-            for observe in (False, True):
-                outs[observe] = self._step_out(o, observe)
-                rets[observe] = HostStepOutput(
-                    reward=_results_view(back, lay, "reward", n),
-                    done=_results_view(back, lay, "done", n).view(torch.bool),
-                    next_action=_results_view(back, lay, "next_action", n),
-                    device=self._step_views(o, observe),
-                )
+            host = {f: _results_view(back, lay, f, n) for f in ("reward", "next_action", "done")}
             d_act = self._alloc((max(n, 1),), torch.int64)
+            io = {
+                "copy": C.SbHostIo(actions_host=None, actions_dev=d_act.data_ptr(), back_dev=o["results"].data_ptr(),
+                                   back_host=back.data_ptr(), back_bytes=lay["bytes"], sync=1, reserved=0),
+                "mapped": C.SbHostIo(actions_host=None, actions_dev=None, back_dev=None, back_host=None, back_bytes=0,
+                                     sync=1, reserved=0),
+            }
+            outs, rets = {"copy": {}, "mapped": {}}, {"copy": {}, "mapped": {}}
+            for observe in (False, True):
+                dev_views = self._step_views(o, observe)
+                outs["copy"][observe] = self._step_out(o, observe)
+                m = self._step_out(o, observe)
+                m.reward, m.done, m.next_action = (host["reward"].data_ptr(), host["done"].data_ptr(),
+                                                   host["next_action"].data_ptr())
+                outs["mapped"][observe] = m
+                for mode in ("copy", "mapped"):
+                    dv = dev_views if mode == "copy" else StepOutput(
+                        **{**dev_views.__dict__, "reward": host["reward"], "done": host["done"].view(torch.bool),
+                           "next_action": host["next_action"]})
+                    rets[mode][observe] = HostStepOutput(reward=host["reward"], done=host["done"].view(torch.bool),
+                                                         next_action=host["next_action"], device=dv)
+            # the per-call path reuses prebuilt ctypes arguments
             self._host = {
-                "back": back, "d_act": d_act, "out": outs, "ret": rets, "pol": {},
-                "act": torch.zeros(max(n, 1), dtype=torch.int64, pin_memory=True)[:n],
-                "io": C.SbHostIo(actions_host=None, actions_dev=d_act.data_ptr(), back_dev=o["results"].data_ptr(),
-                                 back_host=back.data_ptr(), back_bytes=lay["bytes"], sync=1, reserved=0),
+                "back": back, "d_act": d_act, "ret": rets, "pol": {}, "io": io, "shape": torch.Size([n]),
+                "act": torch.zeros(max(n, 1), dtype=torch.int64, pin_memory=True)[:n], "pinned_ptr": None,
+                "fn": C.lib().sb_step_host, "st": ctypes.byref(self._st),
+                "bio": {k: ctypes.byref(v) for k, v in io.items()},
+                "out": {k: {b: ctypes.byref(x) for b, x in v.items()} for k, v in outs.items()}, "outs": outs,
             }
         return self._host
 

@@ -1652,21 +1652,61 @@ int sb_step(const sb_state* s, const int64_t* actions, int64_t ply, const sb_pol
     return launch_env(k, dtype, (cudaStream_t)stream);
 }
 
+// Address through which a kernel reaches p: device and managed memory as
+// is, page-locked host memory through its device mapping; SB_E_ARG for
+// pageable host memory (a kernel touching it would fault).
+static int device_view(const void* p, void** dev) {
+    cudaPointerAttributes at;
+    cudaError_t e = cudaPointerGetAttributes(&at, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(SB_E_ARG, "pointer is neither device memory nor page-locked host memory");
+    }
+    if (at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged) {
+        *dev = const_cast<void*>(p);
+        return SB_OK;
+    }
+    if (at.type != cudaMemoryTypeHost || !at.devicePointer)
+        return fail(SB_E_ARG, "pointer is neither device memory nor page-locked host memory");
+    *dev = at.devicePointer;
+    return SB_OK;
+}
+
 int sb_step_host(const sb_state* s, const sb_host_io* io, int64_t ply, const sb_policy* policy, int auto_reset,
                  const sb_step_out* out, void* stream) {
     int rc = check_state(s);
     if (rc != SB_OK) return rc;
     if (!io) return fail(SB_E_ARG, "io is NULL");
-    if (io->actions_host && !io->actions_dev) return fail(SB_E_ARG, "actions_host needs actions_dev");
     if (io->back_bytes < 0 || (io->back_bytes > 0 && (!io->back_dev || !io->back_host)))
         return fail(SB_E_ARG, "bad copy-back range");
     cudaStream_t st = (cudaStream_t)stream;
-    if (io->actions_host && s->n > 0) {
-        cudaError_t e = cudaMemcpyAsync(io->actions_dev, io->actions_host, (size_t)s->n * sizeof(int64_t),
-                                        cudaMemcpyHostToDevice, st);
-        if (e != cudaSuccess) return cuda_fail(e, "actions host->device");
+    const int64_t* acts = nullptr;
+    if (io->actions_host && io->actions_dev) {
+        if (s->n > 0) {
+            cudaError_t e = cudaMemcpyAsync(io->actions_dev, io->actions_host, (size_t)s->n * sizeof(int64_t),
+                                            cudaMemcpyHostToDevice, st);
+            if (e != cudaSuccess) return cuda_fail(e, "actions host->device");
+        }
+        acts = io->actions_dev;
+    } else if (io->actions_host) {
+        // read in place by the kernel
+        void* d = nullptr;
+        if ((rc = device_view(io->actions_host, &d)) != SB_OK) return rc;
+        acts = static_cast<const int64_t*>(d);
     }
-    rc = sb_step(s, io->actions_host ? io->actions_dev : nullptr, ply, policy, auto_reset, out, stream);
+    sb_step_out o;
+    memset(&o, 0, sizeof o);
+    if (out) o = *out;
+    if (io->back_bytes == 0) {
+        // no copy back: the per-env results may live in page-locked host memory
+        void* d = nullptr;
+        if (o.reward && (rc = device_view(o.reward, &d)) == SB_OK) o.reward = static_cast<float*>(d);
+        if (rc == SB_OK && o.done && (rc = device_view(o.done, &d)) == SB_OK) o.done = static_cast<uint8_t*>(d);
+        if (rc == SB_OK && o.next_action && (rc = device_view(o.next_action, &d)) == SB_OK)
+            o.next_action = static_cast<int16_t*>(d);
+        if (rc != SB_OK) return rc;
+    }
+    rc = sb_step(s, acts, ply, policy, auto_reset, &o, stream);
     if (rc != SB_OK) return rc;
     if (io->back_bytes > 0) {
         cudaError_t e = cudaMemcpyAsync(io->back_host, io->back_dev, (size_t)io->back_bytes,

@@ -269,10 +269,13 @@ def timed_launches(ctx: Ctx, launch, k: int, flush_mib: int):
 def e2e_loop(ctx: Ctx, buf, steps: int, policy: str = "uniform", total_envs: int | None = None
              ) -> tuple[float, int, int]:
     """The public host-side API, ``StrategoRolloutBuffer.step_host``: per step the
-    actions (int64[B], pinned host memory) go host->device, the fused step runs,
-    and reward, done and the next proposed actions come back into pinned host
-    memory with one copy; the call returns once they have landed.  The host
-    takes the proposals as its next actions.  Returns (updates/s, h2d, d2h bytes)."""
+    actions (int64[B], page-locked host memory) cross to the device, the fused
+    step runs, and reward, done and the next proposed actions cross back into
+    page-locked host memory; the call returns once they have landed.  The
+    default transfer is in place (the kernel reads the actions from, and writes
+    the results to, mapped host memory over PCIe: no copy-engine transfers).
+    The host takes the proposals as its next actions.  Returns (updates/s,
+    h2d, d2h bytes)."""
     B = buf.n_games
     h_act = torch.empty(B, dtype=torch.int64, pin_memory=True)
     r = buf.step_host(None, policy=policy)

@@ -153,17 +153,21 @@ int sb_step(const sb_state *s, const int64_t *actions, int64_t ply, const sb_pol
  * in, csrc/stratego_buffer.cpp:70-80; its getters copy back, cpp:300-338). */
 typedef struct sb_host_io {
     const int64_t *actions_host; /* pinned host int64[n], or NULL to sample on the device */
-    int64_t *actions_dev;        /* device int64[n] the host actions are copied into */
+    int64_t *actions_dev;        /* device int64[n] the host actions are copied into; NULL: the
+                                    kernel reads actions_host in place (it must be page-locked
+                                    memory mapped for the device, else SB_E_ARG) */
     const void *back_dev;        /* device range copied to back_host after the step; lay the */
     void *back_host;             /*   step_out fields the host reads (reward, done, next_action) */
-    int64_t back_bytes;          /*   out contiguously so that one copy brings them back */
-    int32_t sync;                /* nonzero: return once the copy back has landed */
+    int64_t back_bytes;          /*   out contiguously so that one copy brings them back (0: no
+                                    copy, e.g. when those step_out fields point at mapped
+                                    page-locked host memory that the kernel writes directly) */
+    int32_t sync;                /* nonzero: return once the step (and copy back) has landed */
     int32_t reserved;
 } sb_host_io;
 
-/* north-star: sb_step with the host copies folded into the same call:
- * actions_host -> actions_dev, the fused ply, back_dev -> back_host, all in
- * stream order on `stream` (three operations, no allocation). */
+/* north-star: sb_step with the host transfers folded into the same call:
+ * actions_host -> actions_dev (or read in place), the fused ply,
+ * back_dev -> back_host, all in stream order on `stream` (no allocation). */
 int sb_step_host(const sb_state *s, const sb_host_io *io, int64_t ply, const sb_policy *policy, int auto_reset,
                  const sb_step_out *out, void *stream);
 

@@ -237,32 +237,33 @@ def test_host_actions_step_equals_reference_api():
     assert_state_equal(export_np(a), export_np(c), "step vs apply_actions")
 
 
-@pytest.mark.parametrize("pinned", [True, False])
-def test_step_host_equals_step(pinned):
+@pytest.mark.parametrize("pinned,mapped", [(True, True), (False, True), (True, False), (False, False)])
+def test_step_host_equals_step(pinned, mapped):
     """sb_step_host (host actions in, reward/done/next_action back into pinned
-    memory in one call) drives the game exactly as step() with device tensors,
-    for host-chosen actions (the previous proposals) and device sampling."""
+    memory in one call: by copies, or read / written in place by the kernel)
+    drives the game exactly as step() with device tensors, for host-chosen
+    actions (the previous proposals) and device sampling."""
     n = 300
     pool = torch.from_numpy(oracle.make_setup_pool(17, 512))
     h = _buf(n, seed=17, setup_pool=pool, no_attack_limit=30)
     d = _buf(n, seed=17, setup_pool=pool, no_attack_limit=30)
     h.reset_all_from_pool()
     d.reset_all_from_pool()
-    r = h.step_host(None)
+    r = h.step_host(None, mapped=mapped)
     ref = d.step(None)
     for t in range(80):
         np.testing.assert_array_equal(r.next_action.numpy(), ref.next_action.cpu().numpy(), err_msg=f"ply {t}")
         np.testing.assert_array_equal(r.reward.numpy(), ref.reward.cpu().numpy())
         np.testing.assert_array_equal(r.done.numpy(), ref.done.cpu().numpy())
         if t % 3 == 2:
-            r, ref = h.step_host(None), d.step(None)
+            r, ref = h.step_host(None, mapped=mapped), d.step(None)
             continue
         acts = r.next_action.to(torch.int64)
         if pinned:
             acts = acts.pin_memory()
         if t % 5 == 0:
             acts[::7] = 0  # illegal: ignored and counted for those games
-        r = h.step_host(acts)
+        r = h.step_host(acts, mapped=mapped)
         ref = d.step(acts.to("cuda"))
         assert torch.equal(r.device.infostate, ref.infostate)
         assert torch.equal(r.device.legal_mask, ref.legal_mask)
@@ -271,6 +272,28 @@ def test_step_host_equals_step(pinned):
         h.step_host(torch.zeros(n, dtype=torch.int64, device="cuda"))
     with pytest.raises(RuntimeError):
         h.step_host(torch.zeros(n - 1, dtype=torch.int64))
+
+
+def test_step_host_rejects_pageable_memory_for_in_place_reads():
+    """The C ABI refuses, with an error and before any launch, a pageable host
+    pointer where the kernel would read in place."""
+    import ctypes
+
+    import ataraxos_b200._capi as C
+
+    n = 64
+    b = _buf(n, seed=3, pool_size=256)
+    b.reset_all_from_pool()
+    h = b._host_io()
+    pageable = np.zeros(n, dtype=np.int64)
+    io = C.SbHostIo(actions_host=pageable.ctypes.data, actions_dev=None, back_dev=None, back_host=None,
+                    back_bytes=0, sync=1, reserved=0)
+    pol = C.SbPolicy(kind=C.SB_POLICY_UNIFORM, reserved=0, logits=None)
+    rc = C.lib().sb_step_host(ctypes.byref(b._st), ctypes.byref(io), 0, ctypes.byref(pol), 1,
+                              h["out"]["copy"][True], torch.cuda.current_stream().cuda_stream)
+    assert rc == C.SB_E_ARG
+    assert b"page-locked" in C.lib().sb_last_error()
+    b.step(None)  # the buffer still works
 
 
 def test_shard_invariance_env_base():
