@@ -692,6 +692,18 @@ class StrategoRolloutBuffer:
         outs["chase_hashes"] = self._ring[: self._n].clone()
         return outs
 
+    def clone(self) -> "StrategoRolloutBuffer":
+        """A new buffer on the same device holding a copy of every game (same
+        seed, env indices, limits, pool and Zobrist table); the two then
+        evolve independently."""
+        c = StrategoRolloutBuffer(
+            self._n, self._device_id, seed=self.seed, env_base=self.env_base, setup_pool=self._pool,
+            no_attack_limit=self.no_attack_limit, max_game_length=self.max_game_length,
+            two_square_limit=self.two_square_limit, zobrist=self._zobrist, obs_dtype=self.obs_dtype,
+            obs_layout=self.obs_layout, mask_format=self.mask_format)
+        c.load_state_dict(self.state_dict())
+        return c
+
     def state_dict(self) -> dict:
         """Everything needed to resume bit-exactly."""
         return {
