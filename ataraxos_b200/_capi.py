@@ -15,9 +15,11 @@ SB_OK, SB_E_ARG, SB_E_CUDA, SB_E_NOPOOL = 0, -1, -2, -3
 SB_DTYPE_F32, SB_DTYPE_BF16 = 0, 1
 SB_LAYOUT_DENSE_ALL, SB_LAYOUT_DENSE_LIVE, SB_LAYOUT_COMPACT = 0, 1, 2
 SB_POLICY_UNIFORM, SB_POLICY_GUMBEL = 0, 1
+SB_RULES_CUDA, SB_RULES_ISF = 0, 1
 SB_STATUS_BAD_SETUP = 1
 SB_STATUS_WAIT_TIMEOUT = 2
 RECORD_BYTES = 256
+ISF_TS_BYTES = 600  # per env under SB_RULES_ISF: 100 squares x 3 intervals x (lo, hi)
 
 vp = ctypes.c_void_p
 
@@ -35,8 +37,9 @@ class SbState(ctypes.Structure):
         ("no_attack_limit", ctypes.c_int32),
         ("max_game_length", ctypes.c_int32),
         ("two_square_limit", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("rules", ctypes.c_int32),
         ("status", vp),
+        ("isf_two_square", vp),
     ]
 
 
@@ -85,7 +88,7 @@ EXPORT_FIELDS = [
     "moves_since_attack", "terminated_since", "moved_squares", "revealed_squares", "move_history",
     "move_history_head", "move_history_len", "two_square_count", "two_square_pair_lo", "two_square_pair_hi",
     "two_square_violation", "chase_hash_head", "chase_hash_len", "chase_last_src", "chasing_violation", "episode",
-    "invalid_count", "reward",
+    "invalid_count", "reward", "isf_two_square", "isf_threats", "isf_evasion",
 ]
 
 
@@ -149,7 +152,7 @@ def lib() -> ctypes.CDLL:
             fn = getattr(handle, name)
             fn.restype = res
             fn.argtypes = args
-        if handle.sb_abi_version() != 1:
+        if handle.sb_abi_version() != 2:
             raise ImportError("libstratego_b200.so ABI version mismatch")
         _lib = handle
     return _lib

@@ -74,6 +74,7 @@ def _raw_stream(index: int) -> int:
 
 
 _POLICIES = {"uniform": C.SB_POLICY_UNIFORM, "gumbel": C.SB_POLICY_GUMBEL}
+_RULES = {"cuda": C.SB_RULES_CUDA, "isf": C.SB_RULES_ISF}
 
 _RESULT_FIELDS = (("reward", torch.float32, 4), ("next_action", torch.int16, 2), ("done", torch.uint8, 1))
 
@@ -139,6 +140,7 @@ class StrategoRolloutBuffer:
         obs_dtype: torch.dtype = torch.bfloat16,
         obs_layout: str = "dense",
         mask_format: str = "u8",
+        rules: str = "cuda",
     ) -> None:
         if n_games < 0:
             raise RuntimeError("n_games must be >= 0")
@@ -158,6 +160,12 @@ class StrategoRolloutBuffer:
         if mask_format not in ("u8", "bits", "none"):
             raise RuntimeError("mask_format must be 'u8', 'bits' or 'none'")
         self.obs_dtype, self.obs_layout, self.mask_format = obs_dtype, obs_layout, mask_format
+        if rules not in _RULES:
+            raise RuntimeError("rules must be 'cuda' (the reference CUDA class's trackers) or 'isf' (the ISF rules "
+                               "of stratego/env/two_square.py and chasing.py)")
+        if rules == "isf" and not 1 <= self.two_square_limit <= 3:
+            raise RuntimeError("rules='isf' supports two_square_limit 1..3")
+        self.rules = rules
         n, dev = self._n, self.device
         with torch.cuda.device(dev):
             self._records = torch.empty((max(n, 1), C.RECORD_BYTES), dtype=torch.uint8, device=dev)
@@ -168,6 +176,9 @@ class StrategoRolloutBuffer:
                 raise RuntimeError("zobrist table must be [10,10,2,13] int64")
             self._zobrist = z.contiguous().to(dev)
             self._status = torch.zeros(1, dtype=torch.int32, device=dev)
+            # per-square two-square state of the ISF rules (none under the CUDA rules)
+            self._isf = (torch.empty((max(n, 1), C.ISF_TS_BYTES), dtype=torch.uint8, device=dev)
+                         if rules == "isf" else None)
             self._pool: torch.Tensor | None = None
             if setup_pool is not None:
                 self.set_setup_pool(setup_pool)
@@ -195,8 +206,9 @@ class StrategoRolloutBuffer:
             no_attack_limit=self.no_attack_limit,
             max_game_length=self.max_game_length,
             two_square_limit=self.two_square_limit,
-            reserved=0,
+            rules=_RULES[self.rules],
             status=self._status.data_ptr(),
+            isf_two_square=_vp(self._isf),
         )
 
     def _call(self, name: str, *args) -> None:
@@ -684,6 +696,8 @@ class StrategoRolloutBuffer:
             "chase_last_src": ((self._n, 2), torch.int32), "chasing_violation": ((self._n,), torch.uint8),
             "episode": ((self._n,), torch.int32), "invalid_count": ((self._n,), torch.int32),
             "reward": ((self._n,), torch.float32),
+            "isf_two_square": ((self._n, 100, 6), torch.uint8), "isf_threats": ((self._n, 2, 4), torch.int8),
+            "isf_evasion": ((self._n, 2), torch.uint8),
         }
         outs = {k: self._alloc(s, d) for k, (s, d) in shapes.items()}
         ex = C.SbExport(**{k: v.data_ptr() for k, v in outs.items()})
@@ -700,7 +714,7 @@ class StrategoRolloutBuffer:
             self._n, self._device_id, seed=self.seed, env_base=self.env_base, setup_pool=self._pool,
             no_attack_limit=self.no_attack_limit, max_game_length=self.max_game_length,
             two_square_limit=self.two_square_limit, zobrist=self._zobrist, obs_dtype=self.obs_dtype,
-            obs_layout=self.obs_layout, mask_format=self.mask_format)
+            obs_layout=self.obs_layout, mask_format=self.mask_format, rules=self.rules)
         c.load_state_dict(self.state_dict())
         return c
 
@@ -715,6 +729,8 @@ class StrategoRolloutBuffer:
             "setup_pool": None if self._pool is None else self._pool.clone(),
             "zobrist": self._zobrist.clone(),
             "limits": (self.no_attack_limit, self.max_game_length, self.two_square_limit),
+            "rules": self.rules,
+            "isf_two_square": None if self._isf is None else self._isf.clone(),
         }
 
     def load_state_dict(self, sd: dict) -> None:
@@ -729,4 +745,8 @@ class StrategoRolloutBuffer:
         self._zobrist.copy_(sd["zobrist"])
         if sd.get("setup_pool") is not None:
             self._pool = sd["setup_pool"].to(self.device).contiguous()
+        if sd.get("rules", "cuda") != self.rules:
+            raise RuntimeError("state_dict was saved from a buffer with other repetition rules")
+        if self._isf is not None:
+            self._isf.copy_(sd["isf_two_square"])
         self._st = self._make_state()

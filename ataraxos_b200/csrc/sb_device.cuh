@@ -58,6 +58,11 @@ constexpr int R_PROPKIND = 166; // u8  policy the cached proposal was drawn with
 constexpr int R_PROPLP = 168;   // f32 log-prob of the cached proposal
 constexpr int R_HIST = 176;     // i16[32] move-history ring
 constexpr int R_BLOOM = 240;    // u64[2] per-side Bloom filter of the chase ring's hashes
+// Under the ISF repetition rules the per-mover two-square fields (120-135)
+// are unused and these take their bytes:
+constexpr int R_ISF_THR = 120;  // i8[2][4] squares each side's last move threatened (-1 none)
+constexpr int R_ISF_EV = 128;   // u8  bit p: side p's last move was an evasion
+constexpr int ISF_TS_BYTES = 600;  // per env: 100 squares x (lo,hi) x 3 segment intersections
 
 constexpr uint8_t C_PIECE = 15, C_BLUE = 16, C_OCC = 32, C_MOVED = 64, C_REV = 128;
 

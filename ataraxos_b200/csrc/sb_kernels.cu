@@ -81,6 +81,8 @@ struct KArgs {
     int32_t n_plies;
     int64_t n_slots;
     int64_t slot0;
+    int32_t rules;  // SB_RULES_*
+    uint8_t* isf;   // [n, ISF_TS_BYTES] under SB_RULES_ISF
 };
 
 constexpr int WARPS = 8;  // warps (envs in flight) per CTA
@@ -329,8 +331,10 @@ __device__ void choose(const KArgs& a, const uint16_t* rays, const int cnt[4], i
 // ---------------------------------------------------------------------------
 
 // zt: the Zobrist table (the CTA's shared-memory copy in env_kernel).
+// isf: the ISF repetition rules are on (a.rules == SB_RULES_ISF; a constant
+// false in the kernel modes that never run them).
 __device__ void reset_env(uint8_t* rec, int64_t* ring2, const KArgs& a, const int64_t* zt, int64_t e, bool from_pool,
-                          int lane) {
+                          int lane, bool isf) {
     const uint8_t* red = nullptr;
     const uint8_t* blue = nullptr;
     const int32_t ep = fld<int32_t>(rec, R_EPISODE);
@@ -378,6 +382,10 @@ __device__ void reset_env(uint8_t* rec, int64_t* ring2, const KArgs& a, const in
     rg[lane] = make_int4(0, 0, 0, 0);
     rg[lane + 32] = make_int4(0, 0, 0, 0);
     if (lane < 4) reinterpret_cast<int4*>(rec + R_HIST)[lane] = make_int4(0, 0, 0, 0);
+    if (isf) {
+        uint2* t = reinterpret_cast<uint2*>(a.isf + e * ISF_TS_BYTES);
+        for (int i = lane; i < ISF_TS_BYTES / 8; i += 32) t[i] = make_uint2(~0u, ~0u);
+    }
     if (lane == 0) {
         fld<int8_t>(rec, R_PLAYER) = 0;
         fld<int8_t>(rec, R_OUTCOME) = -1;
@@ -390,12 +398,17 @@ __device__ void reset_env(uint8_t* rec, int64_t* ring2, const KArgs& a, const in
         rec[R_HLEN] = 0;
         rec[R_TSVIOL] = 0;
         rec[R_CHVIOL] = 0;
-        fld<int32_t>(rec, R_TSCOUNT) = 0;
-        fld<int32_t>(rec, R_TSCOUNT + 4) = 0;
-        fld<int16_t>(rec, R_TSLO) = -1;
-        fld<int16_t>(rec, R_TSLO + 2) = -1;
-        fld<int16_t>(rec, R_TSHI) = -1;
-        fld<int16_t>(rec, R_TSHI + 2) = -1;
+        if (isf) {
+            fld<uint64_t>(rec, R_ISF_THR) = ~0ull;
+            fld<uint64_t>(rec, R_ISF_EV) = ~0ull << 8;  // evasion bits clear, spare bytes 0xFF
+        } else {
+            fld<int32_t>(rec, R_TSCOUNT) = 0;
+            fld<int32_t>(rec, R_TSCOUNT + 4) = 0;
+            fld<int16_t>(rec, R_TSLO) = -1;
+            fld<int16_t>(rec, R_TSLO + 2) = -1;
+            fld<int16_t>(rec, R_TSHI) = -1;
+            fld<int16_t>(rec, R_TSHI + 2) = -1;
+        }
         rec[R_CHHEAD] = 0;
         rec[R_CHHEAD + 1] = 0;
         rec[R_CHLEN] = 0;
@@ -418,14 +431,30 @@ __device__ void reset_env(uint8_t* rec, int64_t* ring2, const KArgs& a, const in
 // Apply one action (csrc/stratego_buffer.cu:111-399)
 // ---------------------------------------------------------------------------
 
+// ISF two-square state: per square the (lo, hi) intervals of one row or
+// column that the piece there covered in its last 1, 2, 3 moves in a row (the
+// intersections of its last k segments), as u16 lo | hi << 8, 0xFFFF when
+// fewer than two squares remain (stratego/env/two_square.py:27-94: the pairs
+// counted k times are exactly the pairs inside that interval).
+__device__ __forceinline__ uint32_t iv_and(uint32_t x, uint32_t y) {
+    if (x == 0xFFFFu || y == 0xFFFFu) return 0xFFFFu;
+    const int xl = x & 0xFF, xh = x >> 8, yl = y & 0xFF, yh = y >> 8;
+    const int xline = xl / 10 == xh / 10 ? xl / 10 : 10 + xl % 10;
+    const int yline = yl / 10 == yh / 10 ? yl / 10 : 10 + yl % 10;
+    if (xline != yline) return 0xFFFFu;
+    const int lo = max(xl, yl), hi = min(xh, yh);
+    return lo < hi ? (uint32_t)(lo | (hi << 8)) : 0xFFFFu;
+}
+
 // Returns false (and changes nothing) when the action is rejected.  On
 // success the board, counters, history, trackers and the caps part of the
 // terminal check are done; check_legal asks the caller for the "side to move
 // has no legal move" test on the new board.
 // The chase ring is read only when the mover's Bloom filter of its hashes
 // (R_BLOOM, cleared with the ring) says the new hash may be in it.
+// tsq: the env's ISF two-square state, or nullptr when the ISF rules are off.
 __device__ bool apply_env(uint8_t* rec, int64_t* ring2, const KArgs& a, const int64_t* zt, int64_t act, int lane,
-                          bool& check_legal, bool& flag_taken) {
+                          bool& check_legal, bool& flag_taken, uint8_t* tsq) {
     check_legal = false;
     flag_taken = false;
     if (act < 0 || act >= NACT) return false;
@@ -484,28 +513,57 @@ __device__ bool apply_env(uint8_t* rec, int64_t* ring2, const KArgs& a, const in
     const int32_t mn = fld<int32_t>(rec, R_MOVENUM) + 1;
     const int head = rec[R_HHEAD], hlen = rec[R_HLEN];
 
-    // two-square, per mover (cu:272-296)
-    int32_t tsc = fld<int32_t>(rec, R_TSCOUNT + 4 * p);
-    int tslo = fld<int16_t>(rec, R_TSLO + 2 * p), tshi = fld<int16_t>(rec, R_TSHI + 2 * p);
+    const bool isf = tsq != nullptr;
+    const uint64_t h_before = fld<uint64_t>(rec, R_ZHASH);
     uint8_t tsv = rec[R_TSVIOL];
-    if (attack) {
-        tsc = 0;
-        tslo = -1;
-        tshi = -1;
-    } else {
-        const int lo = min(src, dst), hi = max(src, dst);
-        if (tslo == lo && tshi == hi) ++tsc;
-        else {
-            tsc = 1;
-            tslo = lo;
-            tshi = hi;
+    uint8_t chv = rec[R_CHVIOL];
+
+    // two-square
+    int32_t tsc = 0;
+    int tslo = -1, tshi = -1;
+    uint32_t isf_new[3] = {0xFFFFu, 0xFFFFu, 0xFFFFu};  // ISF: the entry the piece carries to dst
+    bool isf_keep_dst = false;
+    if (!isf) {
+        // per mover (cu:272-296)
+        tsc = fld<int32_t>(rec, R_TSCOUNT + 4 * p);
+        tslo = fld<int16_t>(rec, R_TSLO + 2 * p);
+        tshi = fld<int16_t>(rec, R_TSHI + 2 * p);
+        if (attack) {
+            tsc = 0;
+            tslo = -1;
+            tshi = -1;
+        } else {
+            const int lo = min(src, dst), hi = max(src, dst);
+            if (tslo == lo && tshi == hi) ++tsc;
+            else {
+                tsc = 1;
+                tslo = lo;
+                tshi = hi;
+            }
+            if (tsc > a.ts_limit) tsv = 1;
         }
-        if (tsc > a.ts_limit) tsv = 1;
+    } else if (!attack) {
+        // per piece (two_square.py:27-63): the move breaks the rule when the
+        // piece's last `limit` segments still share two squares with it
+        const uint16_t* t = reinterpret_cast<const uint16_t*>(tsq) + src * 3;
+        const uint32_t i1 = t[0], i2 = t[1], i3 = t[2];
+        const uint32_t seg = (uint32_t)min(src, dst) | ((uint32_t)max(src, dst) << 8);
+        const uint32_t il = a.ts_limit == 1 ? i1 : (a.ts_limit == 2 ? i2 : i3);
+        if (iv_and(il, seg) != 0xFFFFu) tsv = 1;
+        isf_new[0] = seg;
+        isf_new[1] = iv_and(seg, i1);
+        isf_new[2] = iv_and(seg, i2);
+    } else {
+        // an attack is exempt: the attacker arrives with no counters, a
+        // surviving defender keeps its own
+        isf_keep_dst = result == 2;
     }
 
-    // chasing (cu:306-381): threat = an opponent piece 4-adjacent to dst on
-    // the new board
+    // chasing: the opponent pieces 4-adjacent to dst on the new board
+    // (cu:306-381; chasing.py:115-125), in the order up, down, left, right
     bool threat = false;
+    uint32_t thr = ~0u;
+    int nt = 0;
 #pragma unroll
     for (int d = 0; d < 4; ++d) {
         int q;
@@ -515,31 +573,66 @@ __device__ bool apply_env(uint8_t* rec, int64_t* ring2, const KArgs& a, const in
         else { if (dc == 9) continue; q = dst + 1; }
         if (is_lake(q)) continue;
         const uint8_t c = q == src ? ns : rec[q];
-        if ((c & C_OCC) && ((c >> 4) & 1) == opp) threat = true;
+        if ((c & C_OCC) && ((c >> 4) & 1) == opp) {
+            threat = true;
+            thr = (thr & ~(0xFFu << (8 * nt))) | ((uint32_t)q << (8 * nt));
+            ++nt;
+        }
     }
     int chh = rec[R_CHHEAD + p], chl = rec[R_CHLEN + p], chlast = fld<int8_t>(rec, R_CHLAST + p);
     uint64_t bloom = fld<uint64_t>(rec, R_BLOOM + 8 * p);
-    uint8_t chv = rec[R_CHVIOL];
     int64_t* ring = ring2 + p * NRING;
-    if (threat) {
-        const uint64_t bb = bloom_bits(h);
-        bool found = false;
-        if ((bloom & bb) == bb) {
-            const bool f = (lane < chl && (uint64_t)ring[lane] == h) || (lane + 32 < chl && (uint64_t)ring[lane + 32] == h);
-            found = __any_sync(FULL, f);
-        }
-        bloom |= bb;
-        const bool exc = chlast >= 0 && dst == chlast;
-        if (found && !exc) chv = 1;
-        if (lane == 0) ring[chl < NRING ? chl : chh] = (int64_t)h;
+    auto ring_has = [&](uint64_t x) -> bool {
+        const uint64_t bb = bloom_bits(x);
+        if ((bloom & bb) != bb) return false;
+        const bool f = (lane < chl && (uint64_t)ring[lane] == x) || (lane + 32 < chl && (uint64_t)ring[lane + 32] == x);
+        return __any_sync(FULL, f);
+    };
+    auto ring_add = [&](uint64_t x) {
+        bloom |= bloom_bits(x);
+        if (lane == 0) ring[chl < NRING ? chl : chh] = (int64_t)x;
         if (chl < NRING) ++chl;
         else chh = (chh + 1) % NRING;
-        chlast = src;
+    };
+    uint8_t evb = 0;
+    if (!isf) {
+        // every threatening move is part of the chase; a repeated position
+        // breaks the rule unless dst is the square last left
+        if (threat) {
+            const bool found = ring_has(h);
+            const bool exc = chlast >= 0 && dst == chlast;
+            if (found && !exc) chv = 1;
+            ring_add(h);
+            chlast = src;
+        } else {
+            chl = 0;
+            chh = 0;
+            chlast = -1;
+            bloom = 0;
+        }
     } else {
-        chl = 0;
-        chh = 0;
-        chlast = -1;
-        bloom = 0;
+        // evasion-gated (chasing.py:54-109): a threatening move continues a
+        // chase only when the opponent's last move was an evasion; it breaks
+        // the rule when the board with the mover simply set on dst is already
+        // in the chase and dst is not the square the chaser last left
+        evb = rec[R_ISF_EV];
+        const bool ev_opp = (evb >> opp) & 1;
+        if (threat && ev_opp) {
+            uint64_t hs = h_before ^ zob(zt, src, p, ps) ^ zob(zt, dst, p, ps);
+            if (attack) hs ^= zob(zt, dst, opp, pd);
+            if (ring_has(hs) && !(chlast >= 0 && dst == chlast)) chv = 1;
+            if (!ring_has(h)) ring_add(h);
+            chlast = src;
+        } else if (!threat) {
+            chl = 0;
+            chh = 0;
+            chlast = -1;
+            bloom = 0;
+        }
+        const uint32_t to = fld<uint32_t>(rec, R_ISF_THR + 4 * opp);
+        const bool was_ev = (to & 0xFF) == (uint32_t)src || ((to >> 8) & 0xFF) == (uint32_t)src ||
+                            ((to >> 16) & 0xFF) == (uint32_t)src || (to >> 24) == (uint32_t)src;
+        evb = (uint8_t)((evb & ~(1u << p)) | ((was_ev ? 1u : 0u) << p));
     }
 
     // terminal caps (cu:383-395); the legal-move test is the caller's
@@ -559,9 +652,21 @@ __device__ bool apply_env(uint8_t* rec, int64_t* ring2, const KArgs& a, const in
         rec[R_HHEAD] = (uint8_t)((head + 1) & 31);
         rec[R_HLEN] = (uint8_t)min(hlen + 1, NHIST);
         fld<int8_t>(rec, R_PLAYER) = (int8_t)opp;
-        fld<int32_t>(rec, R_TSCOUNT + 4 * p) = tsc;
-        fld<int16_t>(rec, R_TSLO + 2 * p) = (int16_t)tslo;
-        fld<int16_t>(rec, R_TSHI + 2 * p) = (int16_t)tshi;
+        if (!isf) {
+            fld<int32_t>(rec, R_TSCOUNT + 4 * p) = tsc;
+            fld<int16_t>(rec, R_TSLO + 2 * p) = (int16_t)tslo;
+            fld<int16_t>(rec, R_TSHI + 2 * p) = (int16_t)tshi;
+        } else {
+            fld<uint32_t>(rec, R_ISF_THR + 4 * p) = thr;
+            rec[R_ISF_EV] = evb;
+            uint16_t* t = reinterpret_cast<uint16_t*>(tsq);
+            if (!isf_keep_dst) {
+                t[dst * 3] = (uint16_t)isf_new[0];
+                t[dst * 3 + 1] = (uint16_t)isf_new[1];
+                t[dst * 3 + 2] = (uint16_t)isf_new[2];
+            }
+            t[src * 3] = t[src * 3 + 1] = t[src * 3 + 2] = 0xFFFF;
+        }
         rec[R_TSVIOL] = tsv;
         rec[R_CHHEAD + p] = (uint8_t)chh;
         rec[R_CHLEN + p] = (uint8_t)chl;
@@ -840,6 +945,7 @@ template <typename T, int MODE>
 __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
     constexpr bool kStep = MODE != MODE_GENERIC;
     constexpr bool kProd = MODE == MODE_STEP_PROD;
+    const bool isf_on = !kProd && a.rules == SB_RULES_ISF;  // MODE_STEP_PROD runs the CUDA rules only
     constexpr int kPol = (MODE == MODE_STEP_UNIFORM || kProd) ? SB_POLICY_UNIFORM
                          : (MODE == MODE_STEP_GUMBEL ? SB_POLICY_GUMBEL : -1);
     auto has = [&](uint32_t f) -> bool {
@@ -940,7 +1046,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
 
         if (live && (has(F_RESET_PLANES) || has(F_RESET_POOL)) && (has(F_FORCE) || rec[R_TERM])) {
             zob_wait();
-            reset_env(rec, ring2, a, s_zob, e, has(F_RESET_POOL), lane);
+            reset_env(rec, ring2, a, s_zob, e, has(F_RESET_POOL), lane, isf_on);
             dirty = true;
         }
 
@@ -1003,7 +1109,8 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                     } else {
                         bool chk, flag;
                         zob_wait();
-                        const bool ok = apply_env(rec, ring2, a, s_zob, act, lane, chk, flag);
+                        const bool ok = apply_env(rec, ring2, a, s_zob, act, lane, chk, flag,
+                                                  isf_on ? a.isf + e * ISF_TS_BYTES : nullptr);
                         if (ok) rays_ok = false;  // the board changed
                         if (!ok) {
                             if (lane == 0) fld<int32_t>(rec, R_INVALID) += 1;
@@ -1036,7 +1143,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                 dirty = true;
                 if (has(F_AUTO_RESET) && term) {
                     zob_wait();
-                    reset_env(rec, ring2, a, s_zob, e, true, lane);
+                    reset_env(rec, ring2, a, s_zob, e, true, lane, isf_on);
                     rays_ok = false;
                 }
             }
@@ -1144,7 +1251,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
 // its chase rings start empty (their hashes described the true identities)
 // and its Zobrist hash is recomputed.
 __global__ void __launch_bounds__(WARPS * 32) belief_kernel(const uint8_t* root_rec, int64_t n_roots,
-                                                           const int64_t* root_of, KArgs a) {
+                                                           const int64_t* root_of, KArgs a, const uint8_t* root_isf) {
     __shared__ __align__(16) uint8_t srec[WARPS][REC];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     uint8_t* rec = srec[w];
@@ -1154,6 +1261,12 @@ __global__ void __launch_bounds__(WARPS * 32) belief_kernel(const uint8_t* root_
         const bool bad = r < 0 || r >= n_roots;
         if (bad) r = 0;
         reinterpret_cast<uint2*>(rec)[lane] = reinterpret_cast<const uint2*>(root_rec + r * REC)[lane];
+        if (a.rules == SB_RULES_ISF) {
+            // the per-piece two-square state follows the squares, not the identities
+            const uint2* src = reinterpret_cast<const uint2*>(root_isf + r * ISF_TS_BYTES);
+            uint2* dst = reinterpret_cast<uint2*>(a.isf + e * ISF_TS_BYTES);
+            for (int i = lane; i < ISF_TS_BYTES / 8; i += 32) dst[i] = src[i];
+        }
         __syncwarp();
         const int opp = 1 - rec[R_PLAYER];
         unsigned hid[4], mov[4];
@@ -1260,16 +1373,23 @@ __global__ void hello_kernel(int32_t* out) {
 }
 
 // Fresh-buffer state (csrc/stratego_buffer.cpp:24-55).
-__global__ void init_kernel(uint8_t* rec, int64_t* ring, int64_t n) {
+__global__ void init_kernel(uint8_t* rec, int64_t* ring, int64_t n, int32_t rules, uint8_t* isf) {
     const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (e >= n) return;
     uint8_t* r = rec + e * REC;
     for (int i = 0; i < REC / 16; ++i) reinterpret_cast<int4*>(r)[i] = make_int4(0, 0, 0, 0);
     fld<int8_t>(r, R_OUTCOME) = -1;
-    fld<int16_t>(r, R_TSLO) = -1;
-    fld<int16_t>(r, R_TSLO + 2) = -1;
-    fld<int16_t>(r, R_TSHI) = -1;
-    fld<int16_t>(r, R_TSHI + 2) = -1;
+    if (rules == SB_RULES_ISF) {
+        fld<uint64_t>(r, R_ISF_THR) = ~0ull;
+        fld<uint64_t>(r, R_ISF_EV) = ~0ull << 8;
+        uint2* t = reinterpret_cast<uint2*>(isf + e * ISF_TS_BYTES);
+        for (int i = 0; i < ISF_TS_BYTES / 8; ++i) t[i] = make_uint2(~0u, ~0u);
+    } else {
+        fld<int16_t>(r, R_TSLO) = -1;
+        fld<int16_t>(r, R_TSLO + 2) = -1;
+        fld<int16_t>(r, R_TSHI) = -1;
+        fld<int16_t>(r, R_TSHI + 2) = -1;
+    }
     fld<int8_t>(r, R_CHLAST) = -1;
     fld<int8_t>(r, R_CHLAST + 1) = -1;
     fld<int16_t>(r, R_PROP) = -1;
@@ -1305,7 +1425,7 @@ __global__ void pool_kernel(uint64_t seed, int64_t start, int64_t count, uint8_t
     for (int i = 0; i < 40; ++i) out[t * 40 + i] = p[i];
 }
 
-__global__ void export_kernel(const uint8_t* rec, int64_t n, sb_export o) {
+__global__ void export_kernel(const uint8_t* rec, int64_t n, sb_export o, int32_t rules, const uint8_t* isf) {
     const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (e >= n) return;
     const uint8_t* r = rec + e * REC;
@@ -1328,10 +1448,14 @@ __global__ void export_kernel(const uint8_t* rec, int64_t n, sb_export o) {
         for (int i = 0; i < NHIST; ++i) o.move_history[e * NHIST + i] = *reinterpret_cast<const int16_t*>(r + R_HIST + 2 * i);
     if (o.move_history_head) o.move_history_head[e] = r[R_HHEAD];
     if (o.move_history_len) o.move_history_len[e] = r[R_HLEN];
+    const bool is = rules == SB_RULES_ISF;  // the two rule sets share record bytes 120-135
     for (int p = 0; p < 2; ++p) {
-        if (o.two_square_count) o.two_square_count[e * 2 + p] = *reinterpret_cast<const int32_t*>(r + R_TSCOUNT + 4 * p);
-        if (o.two_square_pair_lo) o.two_square_pair_lo[e * 2 + p] = *reinterpret_cast<const int16_t*>(r + R_TSLO + 2 * p);
-        if (o.two_square_pair_hi) o.two_square_pair_hi[e * 2 + p] = *reinterpret_cast<const int16_t*>(r + R_TSHI + 2 * p);
+        if (o.two_square_count) o.two_square_count[e * 2 + p] = is ? 0 : *reinterpret_cast<const int32_t*>(r + R_TSCOUNT + 4 * p);
+        if (o.two_square_pair_lo) o.two_square_pair_lo[e * 2 + p] = is ? -1 : *reinterpret_cast<const int16_t*>(r + R_TSLO + 2 * p);
+        if (o.two_square_pair_hi) o.two_square_pair_hi[e * 2 + p] = is ? -1 : *reinterpret_cast<const int16_t*>(r + R_TSHI + 2 * p);
+        if (o.isf_evasion) o.isf_evasion[e * 2 + p] = is ? (r[R_ISF_EV] >> p) & 1 : 0;
+        for (int k = 0; k < 4; ++k)
+            if (o.isf_threats) o.isf_threats[e * 8 + p * 4 + k] = is ? *reinterpret_cast<const int8_t*>(r + R_ISF_THR + 4 * p + k) : -1;
         if (o.chase_hash_head) o.chase_hash_head[e * 2 + p] = r[R_CHHEAD + p];
         if (o.chase_hash_len) o.chase_hash_len[e * 2 + p] = r[R_CHLEN + p];
         if (o.chase_last_src) o.chase_last_src[e * 2 + p] = *reinterpret_cast<const int8_t*>(r + R_CHLAST + p);
@@ -1341,6 +1465,8 @@ __global__ void export_kernel(const uint8_t* rec, int64_t n, sb_export o) {
     if (o.episode) o.episode[e] = *reinterpret_cast<const int32_t*>(r + R_EPISODE);
     if (o.invalid_count) o.invalid_count[e] = *reinterpret_cast<const int32_t*>(r + R_INVALID);
     if (o.reward) o.reward[e] = oc == 0 ? 1.0f : (oc == 1 ? -1.0f : 0.0f);
+    if (o.isf_two_square)
+        for (int i = 0; i < ISF_TS_BYTES; ++i) o.isf_two_square[e * ISF_TS_BYTES + i] = is ? isf[e * ISF_TS_BYTES + i] : 0xFF;
 }
 
 __global__ void sum_move_kernel(const uint8_t* rec, int64_t n, int64_t* out) {
@@ -1382,6 +1508,13 @@ int check_state(const sb_state* s) {
     if (!s->records || !s->chase_ring || !s->zobrist) return fail(SB_E_ARG, "records/chase_ring/zobrist is NULL");
     if (!aligned(s->records, 16) || !aligned(s->chase_ring, 16) || !aligned(s->zobrist, 16))
         return fail(SB_E_ARG, "records/chase_ring/zobrist not 16-byte aligned");
+    if (s->rules != SB_RULES_CUDA && s->rules != SB_RULES_ISF) return fail(SB_E_ARG, "unknown repetition rules %d", s->rules);
+    if (s->rules == SB_RULES_ISF) {
+        if (!s->isf_two_square || !aligned(s->isf_two_square, 8))
+            return fail(SB_E_ARG, "SB_RULES_ISF needs an 8-byte aligned isf_two_square [n,600]");
+        if (s->two_square_limit < 1 || s->two_square_limit > 3)
+            return fail(SB_E_ARG, "SB_RULES_ISF supports two-square limits 1..3");
+    }
     if (s->setup_pool && s->pool_size <= 0) return fail(SB_E_ARG, "setup_pool given with pool_size <= 0");
     if (s->pool_size > 0xFFFFFFFFll) return fail(SB_E_ARG, "pool_size above 2^32");
     return SB_OK;
@@ -1402,6 +1535,8 @@ sb::KArgs base_args(const sb_state* s) {
     k.max_len = s->max_game_length;
     k.ts_limit = s->two_square_limit;
     k.status = s->status;
+    k.rules = s->rules;
+    k.isf = s->isf_two_square;
     k.policy = SB_POLICY_UNIFORM;
     k.n_plies = 1;
     k.n_slots = 1;
@@ -1509,7 +1644,8 @@ int launch_env(sb::KArgs& k, int dtype, cudaStream_t st) {
     int mode = sb::MODE_GENERIC;
     if ((k.flags & step) == step && !(k.flags & off)) {
         mode = k.policy == SB_POLICY_UNIFORM ? sb::MODE_STEP_UNIFORM : sb::MODE_STEP_GUMBEL;
-        if (mode == sb::MODE_STEP_UNIFORM && k.n_plies == 1 && (k.flags & (sb::F_INFO | sb::F_MASK_U8)))
+        if (mode == sb::MODE_STEP_UNIFORM && k.n_plies == 1 && (k.flags & (sb::F_INFO | sb::F_MASK_U8)) &&
+            k.rules == SB_RULES_CUDA)
             mode = sb::MODE_STEP_PROD;
     }
     const bool f32 = dtype == SB_DTYPE_F32;
@@ -1558,7 +1694,8 @@ int sb_init_state(const sb_state* s, void* stream) {
     int rc = check_state(s);
     if (rc != SB_OK || s->n == 0) return rc;
     const int64_t blocks = (s->n + 127) / 128;
-    sb::init_kernel<<<(unsigned)blocks, 128, 0, (cudaStream_t)stream>>>(s->records, s->chase_ring, s->n);
+    sb::init_kernel<<<(unsigned)blocks, 128, 0, (cudaStream_t)stream>>>(s->records, s->chase_ring, s->n, s->rules,
+                                                                        s->isf_two_square);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? SB_OK : cuda_fail(e, "init_kernel launch");
 }
@@ -1775,6 +1912,7 @@ int sb_belief_resample(const sb_state* roots, const sb_state* samples, const int
     if (samples->n == 0) return SB_OK;
     if (roots->n < 1) return fail(SB_E_ARG, "no roots");
     if (!root_of) return fail(SB_E_ARG, "root_of is NULL");
+    if (roots->rules != samples->rules) return fail(SB_E_ARG, "roots and samples follow different repetition rules");
     sb::KArgs k = base_args(samples);
     int dev = 0, sms = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -1782,7 +1920,8 @@ int sb_belief_resample(const sb_state* roots, const sb_state* samples, const int
     if ((rc = sm_count(dev, &sms)) != SB_OK) return rc;
     int64_t blocks = (samples->n + sb::WARPS - 1) / sb::WARPS;
     if (blocks > (int64_t)sms * 16) blocks = (int64_t)sms * 16;
-    sb::belief_kernel<<<(unsigned)blocks, sb::WARPS * 32, 0, (cudaStream_t)stream>>>(roots->records, roots->n, root_of, k);
+    sb::belief_kernel<<<(unsigned)blocks, sb::WARPS * 32, 0, (cudaStream_t)stream>>>(roots->records, roots->n, root_of, k,
+                                                                                   roots->isf_two_square);
     e = cudaGetLastError();
     return e == cudaSuccess ? SB_OK : cuda_fail(e, "belief_kernel launch");
 }
@@ -1861,7 +2000,8 @@ int sb_export_state(const sb_state* s, const sb_export* out, void* stream) {
     if (rc != SB_OK || s->n == 0) return rc;
     if (!out) return fail(SB_E_ARG, "out is NULL");
     const int64_t blocks = (s->n + 127) / 128;
-    sb::export_kernel<<<(unsigned)blocks, 128, 0, (cudaStream_t)stream>>>(s->records, s->n, *out);
+    sb::export_kernel<<<(unsigned)blocks, 128, 0, (cudaStream_t)stream>>>(s->records, s->n, *out, s->rules,
+                                                                          s->isf_two_square);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? SB_OK : cuda_fail(e, "export_kernel launch");
 }

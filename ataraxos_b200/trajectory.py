@@ -117,7 +117,7 @@ class BeliefRollouts:
         n = roots.n_games * self.k
         self.samples = StrategoRolloutBuffer(
             n, roots.device_id, seed=seed, zobrist=roots._zobrist.cpu(), no_attack_limit=roots.no_attack_limit,
-            max_game_length=roots.max_game_length, two_square_limit=roots.two_square_limit)
+            max_game_length=roots.max_game_length, two_square_limit=roots.two_square_limit, rules=roots.rules)
         self.root_of = torch.arange(roots.n_games, device=roots.device).repeat_interleave(self.k)
         self.traj = TrajectoryBuffer(self.samples, self.depth + 1, obs_dtype=None, mask_format=mask_format,
                                      policy=policy)

@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define SB_ABI_VERSION 1
+#define SB_ABI_VERSION 2
 #define SB_RECORD_BYTES 256
 #define SB_NUM_SQUARES 100
 #define SB_NUM_ACTIONS 10000
@@ -54,6 +54,14 @@ extern "C" {
 #define SB_LAYOUT_COMPACT 2    /* [n,76,10,10]; plane 43 is a zero pad that the
                                   caller zeroes once */
 
+/* repetition rules (sb_state.rules) */
+#define SB_RULES_CUDA 0        /* the reference CUDA class's trackers: two-square per mover,
+                                  chasing on every threatening move (csrc/stratego_buffer.cu:272-381) */
+#define SB_RULES_ISF 1         /* the reference Python trackers (ISF rules): two-square per piece with
+                                  scout pairs (stratego/env/two_square.py:27-94), chasing gated on the
+                                  opponent's evasions (stratego/env/chasing.py:54-109); needs
+                                  isf_two_square and a two-square limit of 1..3 */
+
 /* action policies for sampling */
 #define SB_POLICY_UNIFORM 0    /* k = (u32 * n_legal) >> 32 over ascending legal actions */
 #define SB_POLICY_GUMBEL 1     /* argmax(logit + Gumbel) over legal actions; logits are
@@ -72,8 +80,10 @@ typedef struct sb_state {
     int32_t no_attack_limit;   /* draw after this many plies without combat (100) */
     int32_t max_game_length;   /* draw at this ply count (4000) */
     int32_t two_square_limit;  /* violation above this many repeats (3) */
-    int32_t reserved;
+    int32_t rules;             /* SB_RULES_* */
     int32_t *status;           /* device word; kernels OR SB_STATUS_* bits in (may be NULL) */
+    uint8_t *isf_two_square;   /* [n,100,6] per-square two-square state of SB_RULES_ISF
+                                  (NULL under SB_RULES_CUDA) */
 } sb_state;
 
 #define SB_STATUS_BAD_SETUP 1   /* a setup plane or pool entry held a piece code > 12 */
@@ -251,6 +261,10 @@ typedef struct sb_export {
     int32_t *episode;           /* [n] */
     int32_t *invalid_count;     /* [n] */
     float *reward;              /* [n] compute_reward_pl0 (cpp:142-151) */
+    uint8_t *isf_two_square;    /* [n,100,6] SB_RULES_ISF per-square segment intersections (lo,hi)
+                                   of the piece's last 1, 2, 3 moves, 255 = none */
+    int8_t *isf_threats;        /* [n,2,4] squares each side's last move threatened, -1 = none */
+    uint8_t *isf_evasion;       /* [n,2] each side's last move was an evasion */
 } sb_export;
 
 int sb_export_state(const sb_state *s, const sb_export *out, void *stream);

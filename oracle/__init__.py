@@ -35,6 +35,7 @@ LIB_PATH = BUILD_DIR / "libstratego_oracle.so"
 
 NSQ, NACT, NHIST, NRING, NCH = 100, 10000, 32, 64, 488
 POLICY_UNIFORM, POLICY_GUMBEL = 0, 1
+RULES_CUDA, RULES_ISF = 0, 1
 
 
 def build(force: bool = False) -> Path:
@@ -65,6 +66,8 @@ class _OState(ctypes.Structure):
         ("chase", ctypes.c_void_p), ("chase_head", ctypes.c_void_p), ("chase_len", ctypes.c_void_p),
         ("chase_last_src", ctypes.c_void_p), ("chase_violation", ctypes.c_void_p),
         ("episode", ctypes.c_void_p), ("invalid_count", ctypes.c_void_p),
+        ("isf_ts", ctypes.c_void_p), ("isf_threats", ctypes.c_void_p), ("isf_evasion", ctypes.c_void_p),
+        ("isf_event", ctypes.c_void_p),
     ]
 
 
@@ -74,7 +77,7 @@ class _OConfig(ctypes.Structure):
         ("no_attack_limit", ctypes.c_int32),
         ("max_game_length", ctypes.c_int32),
         ("two_square_limit", ctypes.c_int32),
-        ("pad_", ctypes.c_int32),
+        ("rules", ctypes.c_int32),
         ("seed", ctypes.c_uint64),
         ("env_base", ctypes.c_int64),
         ("pool", ctypes.c_void_p),
@@ -173,6 +176,13 @@ STATE_FIELDS = {
     "chasing_violation": (np.uint8, (), 0),
     "episode": (np.int32, (), 0),
     "invalid_count": (np.int32, (), 0),
+    # ISF repetition rules (rules=RULES_ISF): per-square two-square segment
+    # intersections (lo, hi) for the last 1, 2, 3 moves (255 = none), the
+    # squares each side's last move threatened (-1 = none), and whether it
+    # was an evasion
+    "isf_two_square": (np.uint8, (NSQ, 6), 255),
+    "isf_threats": (np.int8, (2, 4), -1),
+    "isf_evasion": (np.uint8, (2,), 0),
 }
 
 _CFIELD = {
@@ -184,6 +194,7 @@ _CFIELD = {
     "two_square_pair_hi": "ts_hi", "two_square_violation": "ts_violation", "chase_hashes": "chase",
     "chase_hash_head": "chase_head", "chase_hash_len": "chase_len", "chase_last_src": "chase_last_src",
     "chasing_violation": "chase_violation", "episode": "episode", "invalid_count": "invalid_count",
+    "isf_two_square": "isf_ts", "isf_threats": "isf_threats", "isf_evasion": "isf_evasion",
 }
 
 
@@ -201,12 +212,19 @@ class OracleState:
         two_square_limit: int = 3,
         zobrist: np.ndarray | None = None,
         pool: np.ndarray | None = None,
+        rules: int = RULES_CUDA,
     ) -> None:
+        if rules == RULES_ISF and not 1 <= two_square_limit <= 3:
+            raise ValueError("the ISF two-square tracker supports limits 1..3")
         self.n = int(n)
         self.a: dict[str, np.ndarray] = {}
         for name, (dt, shp, init) in STATE_FIELDS.items():
             self.a[name] = np.full((self.n, *shp), init, dtype=dt)
-        self._st = _OState(n=self.n, **{_CFIELD[k]: _ptr(v) for k, v in self.a.items()})
+        # rules the last applied move broke (bit 0 two-square, bit 1 chasing);
+        # oracle-only, for checking against the reference's trackers move by move
+        self.isf_event = np.zeros(self.n, dtype=np.uint8)
+        self._st = _OState(n=self.n, isf_event=_ptr(self.isf_event),
+                           **{_CFIELD[k]: _ptr(v) for k, v in self.a.items()})
         self.zobrist = np.ascontiguousarray(zobrist_table() if zobrist is None else zobrist, dtype=np.int64)
         self.pool = None if pool is None else np.ascontiguousarray(pool, dtype=np.uint8)
         self._cfg = _OConfig(
@@ -218,6 +236,7 @@ class OracleState:
             env_base=env_base,
             pool=_ptr(self.pool),
             pool_size=0 if self.pool is None else len(self.pool),
+            rules=rules,
         )
         self.ply = 0
 

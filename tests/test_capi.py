@@ -24,7 +24,7 @@ def declared_functions() -> list[str]:
 
 def test_library_loads_and_reports_abi():
     lib = C.lib()
-    assert lib.sb_abi_version() == 1
+    assert lib.sb_abi_version() == 2
     assert Path(C.LIB_PATH).exists()
 
 
