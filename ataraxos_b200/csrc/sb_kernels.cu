@@ -739,6 +739,10 @@ struct Quad<uint16_t> {
         return make_uint2(p2, p2);
     }
     static __device__ __forceinline__ V orv(V a, V b) { return make_uint2(a.x | b.x, a.y | b.y); }
+    // element pattern `pat` where byte j of m is 1, 0 where it is 0
+    static __device__ __forceinline__ V ones(uint32_t m, uint32_t pat) {
+        return make_uint2(__byte_perm(m, 0, 0x4140) * pat, __byte_perm(m, 0, 0x4342) * pat);
+    }
     static __device__ __forceinline__ void st(uint8_t* p, V v) { *reinterpret_cast<uint2*>(p) = v; }
     static __device__ __forceinline__ uint32_t bits(uint16_t v) { return v; }
 };
@@ -751,6 +755,9 @@ struct Quad<float> {
     }
     static __device__ __forceinline__ V splat(uint32_t pat) { return make_uint4(pat, pat, pat, pat); }
     static __device__ __forceinline__ V orv(V a, V b) { return make_uint4(a.x | b.x, a.y | b.y, a.z | b.z, a.w | b.w); }
+    static __device__ __forceinline__ V ones(uint32_t m, uint32_t pat) {
+        return make_uint4((m & 0xFF) * pat, ((m >> 8) & 0xFF) * pat, ((m >> 16) & 0xFF) * pat, (m >> 24) * pat);
+    }
     static __device__ __forceinline__ void st(uint8_t* p, V v) { *reinterpret_cast<uint4*>(p) = v; }
     static __device__ __forceinline__ uint32_t bits(float v) { return __float_as_uint(v); }
 };
@@ -788,7 +795,12 @@ __device__ __forceinline__ SqFeat square_features(const uint8_t* rec, int lane) 
     return f;
 }
 
-// Dense planes 12-42, computed in full (lanes 0..24).
+// Dense planes 12-42 (lanes 0..24).  Planes 12-35 hold, per side, 1/12 on
+// every hidden piece of that side in all 12 rows and 1 on a revealed piece in
+// its type's row: each lane stores the hidden-piece background in all 24 rows
+// (the same two words for 12 rows, no per-row arithmetic), then sets the few
+// revealed squares of its 4 squares to 1 with scalar stores (same thread, so
+// the later store wins).  Planes 36-40 are flag rows, 41-42 constants.
 template <typename T>
 __device__ void write_info_dense(const uint8_t* rec, const KArgs& a, int lane, uint8_t* g) {
     if (lane >= 25) return;
@@ -798,19 +810,24 @@ __device__ void write_info_dense(const uint8_t* rec, const KArgs& a, int lane, u
     const uint32_t ONE = Q::bits(IV<T>::from(1.0f));
     const uint32_t TW = Q::bits(IV<T>::from(__fdiv_rn(1.0f, 12.0f)));
     uint8_t* gl = g + lane * 4 * (int)sizeof(T);
-    // 12-23: opponent, 1/12 where hidden, one-hot where revealed
-    const typename Q::V hid_o = Q::sel(__vcmpne4(f.fl & 0x02020202u, 0u), TW);
-#pragma unroll 1
-    for (int t = 0; t < 12; ++t)
-        Q::st(gl + (12 + t) * PB, Q::orv(Q::sel(__vcmpeq4(f.ort, (uint32_t)(t + 1) * 0x01010101u), ONE), hid_o));
-    // 24-35: own pieces as the opponent sees them
-    const typename Q::V hid_w = Q::sel(__vcmpne4(f.fl & 0x01010101u, 0u), TW);
-#pragma unroll 1
-    for (int t = 0; t < 12; ++t)
-        Q::st(gl + (24 + t) * PB, Q::orv(Q::sel(__vcmpeq4(f.owt, (uint32_t)(t + 1) * 0x01010101u), ONE), hid_w));
+    const typename Q::V hid_o = Q::ones((f.fl >> 1) & 0x01010101u, TW);  // opponent hidden
+    const typename Q::V hid_w = Q::ones(f.fl & 0x01010101u, TW);         // own hidden
+#pragma unroll
+    for (int t = 0; t < 12; ++t) {
+        Q::st(gl + (12 + t) * PB, hid_o);
+        Q::st(gl + (24 + t) * PB, hid_w);
+    }
+    T* gl1 = reinterpret_cast<T*>(gl);
+    const T one = IV<T>::from(1.0f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t to = (f.ort >> (8 * j)) & 0xFF, tw = (f.owt >> (8 * j)) & 0xFF;
+        if (to) gl1[(11 + to) * NSQ + j] = one;  // 12-23: opponent revealed, one-hot
+        if (tw) gl1[(23 + tw) * NSQ + j] = one;  // 24-35: own pieces the opponent has seen
+    }
     // 36 own hidden, 37 opponent hidden, 38 empty (lakes included), 39 own moved, 40 opponent moved
-#pragma unroll 1
-    for (int i = 0; i < 5; ++i) Q::st(gl + (36 + i) * PB, Q::sel(__vcmpne4(f.fl & ((1u << i) * 0x01010101u), 0u), ONE));
+#pragma unroll
+    for (int i = 0; i < 5; ++i) Q::st(gl + (36 + i) * PB, Q::ones((f.fl >> i) & 0x01010101u, ONE));
     // 41 / 42: the two fractions (exact float32 quotients)
     const int mn = fld<int32_t>(rec, R_MOVENUM), msa = fld<int32_t>(rec, R_MSA);
     Q::st(gl + 41 * PB, Q::splat(Q::bits(IV<T>::from(a.max_len > 0 ? __fdiv_rn((float)mn, (float)a.max_len) : 0.0f))));
@@ -932,22 +949,26 @@ __device__ void write_mask_bits(const uint32_t* w, int lane, uint8_t* g) {
 // apply + step + propose (and the policy) at compile time so that the hot
 // kernel carries only the code it runs.
 constexpr int MODE_GENERIC = 0, MODE_STEP_UNIFORM = 1, MODE_STEP_GUMBEL = 2, MODE_STEP_PROD = 3;
+// added to a step mode: the kernel also carries the ISF repetition rules
+// (the generic kernel always does; the CUDA-rules step kernels never pay for them)
+constexpr int MODE_ISF = 8;
 // MODE_STEP_PROD is MODE_STEP_UNIFORM for a single ply with a u8 mask and /
 // or an infostate (the config-2 step).  There every env's game logic runs in
 // one wave at the same time, so HBM would idle through it: each 8-warp CTA
 // gives one warp to a producer that streams the envs' zero rows with bulk
-// copies while the other 7 play; named barrier 1 orders the completed zero
-// rows before the one-hots stored on top, barrier 2 orders the one-hots of a
-// batch before the producer's next bulk writes.  Multi-ply and Gumbel
-// launches keep all 8 warps on envs (measured faster there).
+// copies while the other 7 play; an mbarrier orders the completed zero rows
+// before the one-hots stored on top, a second one keeps the producer at most
+// one batch ahead.  Multi-ply and Gumbel launches keep all 8 warps on envs
+// (measured faster there).
 
 template <typename T, int MODE>
 __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
-    constexpr bool kStep = MODE != MODE_GENERIC;
-    constexpr bool kProd = MODE == MODE_STEP_PROD;
-    const bool isf_on = !kProd && a.rules == SB_RULES_ISF;  // MODE_STEP_PROD runs the CUDA rules only
-    constexpr int kPol = (MODE == MODE_STEP_UNIFORM || kProd) ? SB_POLICY_UNIFORM
-                         : (MODE == MODE_STEP_GUMBEL ? SB_POLICY_GUMBEL : -1);
+    constexpr int M = MODE & ~MODE_ISF;
+    constexpr bool kStep = M != MODE_GENERIC;
+    constexpr bool kProd = M == MODE_STEP_PROD;
+    const bool isf_on = (M == MODE_GENERIC || (MODE & MODE_ISF) != 0) && a.rules == SB_RULES_ISF;
+    constexpr int kPol = (M == MODE_STEP_UNIFORM || kProd) ? SB_POLICY_UNIFORM
+                         : (M == MODE_STEP_GUMBEL ? SB_POLICY_GUMBEL : -1);
     auto has = [&](uint32_t f) -> bool {
         if (kStep) {
             if (f & (F_RESET_PLANES | F_RESET_POOL | F_SAMPLE_OUT | F_HAS_LEGAL)) return false;
@@ -1647,13 +1668,19 @@ int launch_env(sb::KArgs& k, int dtype, cudaStream_t st) {
         if (mode == sb::MODE_STEP_UNIFORM && k.n_plies == 1 && (k.flags & (sb::F_INFO | sb::F_MASK_U8)) &&
             k.rules == SB_RULES_CUDA)
             mode = sb::MODE_STEP_PROD;
+        if (k.rules == SB_RULES_ISF) mode |= sb::MODE_ISF;
     }
     const bool f32 = dtype == SB_DTYPE_F32;
+    constexpr int UI = sb::MODE_STEP_UNIFORM | sb::MODE_ISF, GI = sb::MODE_STEP_GUMBEL | sb::MODE_ISF;
     switch (mode) {
         case sb::MODE_STEP_UNIFORM:
             return f32 ? launch_mode<float, sb::MODE_STEP_UNIFORM>(k, st) : launch_mode<uint16_t, sb::MODE_STEP_UNIFORM>(k, st);
         case sb::MODE_STEP_GUMBEL:
             return f32 ? launch_mode<float, sb::MODE_STEP_GUMBEL>(k, st) : launch_mode<uint16_t, sb::MODE_STEP_GUMBEL>(k, st);
+        case UI:
+            return f32 ? launch_mode<float, UI>(k, st) : launch_mode<uint16_t, UI>(k, st);
+        case GI:
+            return f32 ? launch_mode<float, GI>(k, st) : launch_mode<uint16_t, GI>(k, st);
         case sb::MODE_STEP_PROD:
             return f32 ? launch_mode<float, sb::MODE_STEP_PROD>(k, st) : launch_mode<uint16_t, sb::MODE_STEP_PROD>(k, st);
         default:
