@@ -152,22 +152,28 @@ __device__ __noinline__ void enumerate(const uint8_t* b, int p, uint16_t* rays, 
         ownT[k] = __ballot_sync(FULL, ctm);
         oppT[k] = __ballot_sync(FULL, cto && !ctm);
     }
-    const uint32_t S0 = own[0] | lake_word(0), S1 = own[1] | lake_word(1), S2 = own[2] | lake_word(2), S3 = own[3] | lake_word(3);
-    const uint32_t T0 = ownT[0] | lake_word_t(0), T1 = ownT[1] | lake_word_t(1), T2 = ownT[2] | lake_word_t(2),
-                   T3 = ownT[3] | lake_word_t(3);
+    // lane l (l = lane % 10) extracts row l and column l as 10-bit lines,
+    // stoppers | enemies << 16; every square then fetches its row and column
+    // line with one shuffle each instead of extracting them itself
+    const int l = lane % 10;
+    const uint32_t rw = line10(own[0] | lake_word(0), own[1] | lake_word(1), own[2] | lake_word(2),
+                               own[3] | lake_word(3), 10 * l) |
+                        (line10(opp[0], opp[1], opp[2], opp[3], 10 * l) << 16);
+    const uint32_t cw = line10(ownT[0] | lake_word_t(0), ownT[1] | lake_word_t(1), ownT[2] | lake_word_t(2),
+                               ownT[3] | lake_word_t(3), 10 * l) |
+                        (line10(oppT[0], oppT[1], oppT[2], oppT[3], 10 * l) << 16);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int sq = lane + 32 * k;
+        const int r = sq / 10, col = sq - 10 * r;
+        const uint32_t rl = __shfl_sync(FULL, rw, r < 10 ? r : 0), cl = __shfl_sync(FULL, cw, col);
         cnt[k] = 0;
         if (sq < NSQ) {
             const uint8_t c = code[k];
             const int pc = c & C_PIECE;
             uint16_t packed = 0;
             if ((c & C_OCC) && ((c >> 4) & 1) == p && can_move(pc)) {
-                const int r = sq / 10, col = sq - 10 * r;
-                const uint32_t rs = line10(S0, S1, S2, S3, 10 * r), re = line10(opp[0], opp[1], opp[2], opp[3], 10 * r);
-                const uint32_t cs = line10(T0, T1, T2, T3, 10 * col);
-                const uint32_t ce = line10(oppT[0], oppT[1], oppT[2], oppT[3], 10 * col);
+                const uint32_t rs = rl & 0x3FFu, re = rl >> 16, cs = cl & 0x3FFu, ce = cl >> 16;
                 int up = ray_back(cs, ce, r), down = ray_fwd(cs, ce, r);
                 int left = ray_back(rs, re, col), right = ray_fwd(rs, re, col);
                 if (pc != 2) {
@@ -775,23 +781,20 @@ struct Quad<float> {
 struct SqFeat {
     uint32_t ot, ort, owt, fl;  // own type, opponent revealed type, own revealed type, flag bits
 };
+// Byte-parallel over the lane's 4 square codes: each field is a byte mask.
 __device__ __forceinline__ SqFeat square_features(const uint8_t* rec, int lane) {
-    const int p = rec[R_PLAYER];
+    constexpr uint32_t B1 = 0x01010101u;
+    const uint32_t prep = rec[R_PLAYER] ? B1 : 0u;
     const uint32_t codes = *reinterpret_cast<const uint32_t*>(rec + 4 * lane);
-    SqFeat f{0, 0, 0, 0};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const uint32_t c = (codes >> (8 * j)) & 0xFF;
-        const bool occ = c & C_OCC, rev = c & C_REV, mov = c & C_MOVED;
-        const bool own = occ && ((c >> 4) & 1) == (uint32_t)p, opp = occ && !own;
-        const uint32_t pc = c & C_PIECE;
-        f.ot |= (own ? pc : 0u) << (8 * j);
-        f.ort |= (opp && rev ? pc : 0u) << (8 * j);
-        f.owt |= (own && rev ? pc : 0u) << (8 * j);
-        const uint32_t b = (own && !rev ? 1u : 0u) | (opp && !rev ? 2u : 0u) | (!occ ? 4u : 0u) | (own && mov ? 8u : 0u) |
-                           (opp && mov ? 16u : 0u);
-        f.fl |= b << (8 * j);
-    }
+    const uint32_t occ = (codes >> 5) & B1, blue = (codes >> 4) & B1;
+    const uint32_t rev = (codes >> 7) & B1, mov = (codes >> 6) & B1;
+    const uint32_t own = occ & ~(blue ^ prep), opp = occ ^ own;  // 0/1 per byte
+    const uint32_t pc = codes & 0x0F0F0F0Fu;
+    SqFeat f;
+    f.ot = pc & (own * 0xFFu);
+    f.ort = pc & ((opp & rev) * 0xFFu);
+    f.owt = pc & ((own & rev) * 0xFFu);
+    f.fl = (own & ~rev) | ((opp & ~rev) << 1) | ((occ ^ B1) << 2) | ((own & mov) << 3) | ((opp & mov) << 4);
     return f;
 }
 
