@@ -131,30 +131,46 @@ __device__ __forceinline__ int ray_back(uint32_t S, uint32_t E, int x) {
     return (x - 1 - h) + (int)((E >> h) & 1u);
 }
 
-// Ray lengths of every lane square for side p, packed as up | left<<4 |
-// right<<8 | down<<12 (the groups in ascending destination order) into
-// rays[], and the per-square counts.
-// Not inlined: its three call sites share one copy of the code, which keeps
-// the step kernel's instruction footprint small.
-__device__ __noinline__ void enumerate(const uint8_t* b, int p, uint16_t* rays, int lane, int cnt[4]) {
-    uint32_t own[4], opp[4], ownT[4], oppT[4];
-    uint8_t code[4];
+// Position of the k-th (0-based) set bit of m (popcount bisection).
+__device__ __forceinline__ int nth_bit(uint32_t m, int k) {
+    int pos = 0, c = __popc(m & 0xFFFFu);
+    if (k >= c) { k -= c; m >>= 16; pos += 16; }
+    c = __popc(m & 0xFFu);
+    if (k >= c) { k -= c; m >>= 8; pos += 8; }
+    c = __popc(m & 0xFu);
+    if (k >= c) { k -= c; m >>= 4; pos += 4; }
+    c = __popc(m & 0x3u);
+    if (k >= c) { k -= c; m >>= 2; pos += 2; }
+    return pos + (k >= (int)(m & 1u) ? 1 : 0);
+}
+
+// Ray lengths of every square for side p, packed as up | left<<4 | right<<8
+// | down<<12 (the groups in ascending destination order) into rays[] (0 for
+// squares without a movable piece of side p); returns the number of legal
+// moves (warp-uniform).  The rays are computed per movable piece: lane i
+// takes the i-th movable piece in ascending square order (a second round
+// when there are more than 32), so the ray arithmetic runs once or twice
+// per warp instead of once per 32-square block.
+// Not inlined: its call sites share one copy of the code, which keeps the
+// step kernel's instruction footprint small.
+__device__ __noinline__ int enumerate(const uint8_t* b, int p, uint16_t* rays, int lane) {
+    uint32_t own[4], opp[4], ownT[4], oppT[4], mv[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int i = lane + 32 * k;
         const uint8_t c = i < NSQ ? b[i] : 0;
         const uint8_t ct = i < NSQ ? b[(i % 10) * 10 + i / 10] : 0;
-        code[k] = c;
         const bool co = c & C_OCC, cto = ct & C_OCC;
         const bool cm = co && ((c >> 4) & 1) == p, ctm = cto && ((ct >> 4) & 1) == p;
         own[k] = __ballot_sync(FULL, cm);
         opp[k] = __ballot_sync(FULL, co && !cm);
         ownT[k] = __ballot_sync(FULL, ctm);
         oppT[k] = __ballot_sync(FULL, cto && !ctm);
+        mv[k] = __ballot_sync(FULL, cm && can_move(c & C_PIECE));
     }
     // lane l (l = lane % 10) extracts row l and column l as 10-bit lines,
-    // stoppers | enemies << 16; every square then fetches its row and column
-    // line with one shuffle each instead of extracting them itself
+    // stoppers | enemies << 16; a piece fetches its row and column line with
+    // one shuffle each
     const int l = lane % 10;
     const uint32_t rw = line10(own[0] | lake_word(0), own[1] | lake_word(1), own[2] | lake_word(2),
                                own[3] | lake_word(3), 10 * l) |
@@ -162,33 +178,49 @@ __device__ __noinline__ void enumerate(const uint8_t* b, int p, uint16_t* rays, 
     const uint32_t cw = line10(ownT[0] | lake_word_t(0), ownT[1] | lake_word_t(1), ownT[2] | lake_word_t(2),
                                ownT[3] | lake_word_t(3), 10 * l) |
                         (line10(oppT[0], oppT[1], oppT[2], oppT[3], 10 * l) << 16);
+    for (int i = lane; i < NSQ / 2; i += 32) reinterpret_cast<uint32_t*>(rays)[i] = 0u;
+    __syncwarp();
+    const int c0 = __popc(mv[0]), c01 = c0 + __popc(mv[1]), c012 = c01 + __popc(mv[2]);
+    const int npieces = c012 + __popc(mv[3]);
+    int total = 0;
+    for (int base = 0; base < npieces; base += 32) {
+        const int i = base + lane;
+        int sq = -1;
+        if (i < npieces) {
+            const int w = i < c0 ? 0 : (i < c01 ? 1 : (i < c012 ? 2 : 3));
+            const int k = i - (w == 0 ? 0 : (w == 1 ? c0 : (w == 2 ? c01 : c012)));
+            const uint32_t m = w == 0 ? mv[0] : (w == 1 ? mv[1] : (w == 2 ? mv[2] : mv[3]));
+            sq = 32 * w + nth_bit(m, k);
+        }
+        const int r = sq >= 0 ? sq / 10 : 0, col = sq >= 0 ? sq - 10 * r : 0;
+        const uint32_t rl = __shfl_sync(FULL, rw, r), cl = __shfl_sync(FULL, cw, col);
+        if (sq >= 0) {
+            const uint32_t rs = rl & 0x3FFu, re = rl >> 16, cs = cl & 0x3FFu, ce = cl >> 16;
+            int up = ray_back(cs, ce, r), down = ray_fwd(cs, ce, r);
+            int left = ray_back(rs, re, col), right = ray_fwd(rs, re, col);
+            if ((b[sq] & C_PIECE) != 2) {
+                up = min(up, 1);
+                down = min(down, 1);
+                left = min(left, 1);
+                right = min(right, 1);
+            }
+            rays[sq] = (uint16_t)(up | (left << 4) | (right << 8) | (down << 12));
+            total += up + left + right + down;
+        }
+    }
+    total = warp_sum(total);
+    __syncwarp();
+    return total;
+}
+
+// Moves of a packed ray set, and of the lane's four squares.
+__device__ __forceinline__ int ray_count(uint32_t r) { return (r & 15) + ((r >> 4) & 15) + ((r >> 8) & 15) + (r >> 12); }
+__device__ __forceinline__ void ray_counts(const uint16_t* rays, int lane, int cnt[4]) {
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int sq = lane + 32 * k;
-        const int r = sq / 10, col = sq - 10 * r;
-        const uint32_t rl = __shfl_sync(FULL, rw, r < 10 ? r : 0), cl = __shfl_sync(FULL, cw, col);
-        cnt[k] = 0;
-        if (sq < NSQ) {
-            const uint8_t c = code[k];
-            const int pc = c & C_PIECE;
-            uint16_t packed = 0;
-            if ((c & C_OCC) && ((c >> 4) & 1) == p && can_move(pc)) {
-                const uint32_t rs = rl & 0x3FFu, re = rl >> 16, cs = cl & 0x3FFu, ce = cl >> 16;
-                int up = ray_back(cs, ce, r), down = ray_fwd(cs, ce, r);
-                int left = ray_back(rs, re, col), right = ray_fwd(rs, re, col);
-                if (pc != 2) {
-                    up = min(up, 1);
-                    down = min(down, 1);
-                    left = min(left, 1);
-                    right = min(right, 1);
-                }
-                packed = (uint16_t)(up | (left << 4) | (right << 8) | (down << 12));
-                cnt[k] = up + left + right + down;
-            }
-            rays[sq] = packed;
-        }
+        cnt[k] = sq < NSQ ? ray_count(rays[sq]) : 0;
     }
-    __syncwarp();
 }
 
 // j-th destination (0-based, ascending) of a packed ray set.
@@ -205,7 +237,9 @@ __device__ __forceinline__ int decode_ray(int sq, uint32_t r, int j) {
 
 // kth legal action in ascending src*100+dst order (warp-uniform result).
 // The four 32-square blocks are scanned together, two 16-bit sums per word.
-__device__ int kth_action(int kth, const int cnt[4], const uint16_t* rays, int lane) {
+__device__ int kth_action(int kth, const uint16_t* rays, int lane) {
+    int cnt[4];
+    ray_counts(rays, lane, cnt);
     uint32_t a01 = (uint32_t)cnt[0] | ((uint32_t)cnt[1] << 16), a23 = (uint32_t)cnt[2] | ((uint32_t)cnt[3] << 16);
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -230,7 +264,6 @@ __device__ int kth_action(int kth, const int cnt[4], const uint16_t* rays, int l
     return sq * 100 + decode_ray(sq, rays[sq], kth - base - excl);
 }
 
-__device__ __forceinline__ int count_of(const int cnt[4]) { return warp_sum(cnt[0] + cnt[1] + cnt[2] + cnt[3]); }
 
 // Virtual N(0,1) logit (Box-Muller) and Gumbel noise of action `act`.
 __device__ __forceinline__ void logit_noise(uint64_t seed, int64_t ge, int64_t ply, int act, float& z, float& g) {
@@ -240,12 +273,12 @@ __device__ __forceinline__ void logit_noise(uint64_t seed, int64_t ge, int64_t p
     g = -logf(-logf(u3));
 }
 
-// Choose an action for the current state (rays/cnt already enumerated).
+// Choose an action for the current state (rays already enumerated, n moves).
 // Uniform: k = (u32 * n) >> 32 over ascending legal actions.  Gumbel: argmax
 // of logit + Gumbel over legal actions, ties to the smaller action index.
 // u_pre: the uniform policy's Philox word when the caller drew it already.
 template <int POL>
-__device__ void choose(const KArgs& a, const uint16_t* rays, const int cnt[4], int n, int64_t e, int64_t ply,
+__device__ void choose(const KArgs& a, const uint16_t* rays, int n, int64_t e, int64_t ply,
                        int lane, int& act, float& lp, int16_t* acts = nullptr, const uint32_t* u_pre = nullptr) {
     const int64_t ge = a.env_base + e;
     if (n == 0) {
@@ -257,10 +290,12 @@ __device__ void choose(const KArgs& a, const uint16_t* rays, const int cnt[4], i
     if (pol == SB_POLICY_UNIFORM) {
         const uint32_t u =
             u_pre ? *u_pre : philox((uint32_t)ge, (uint32_t)ply, (uint32_t)((uint64_t)ply >> 32), TAG_ACTION, a.seed).x;
-        act = kth_action((int)mulshift(u, (uint32_t)n), cnt, rays, lane);
+        act = kth_action((int)mulshift(u, (uint32_t)n), rays, lane);
         lp = -logf((float)n);
         return;
     }
+    int cnt[4];
+    ray_counts(rays, lane, cnt);
     float best = -INFINITY, bestz = 0.0f, m = -INFINITY, s = 0.0f;
     int besta = 0x7fffffff;
     auto visit = [&](int ac) {
@@ -1065,8 +1100,8 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
         }
         int64_t* ring2 = a.ring + e * 2 * NRING;
         bool dirty = false;
-        bool rays_ok = false;  // rays/cnt describe the side to move of the current board
-        int cnt[4] = {0, 0, 0, 0};
+        bool rays_ok = false;  // rays / n_moves describe the side to move of the current board
+        int n_moves = 0;
 
         if (live && (has(F_RESET_PLANES) || has(F_RESET_POOL)) && (has(F_FORCE) || rec[R_TERM])) {
             zob_wait();
@@ -1111,11 +1146,10 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                                 lp = fld<float>(rec, R_PROPLP);
                             }
                         } else {
-                            enumerate(rec, pm, rays, lane, cnt);
-                            n_legal = count_of(cnt);
+                            n_legal = enumerate(rec, pm, rays, lane);
                             if (!a.actions) {
                                 int ac;
-                                choose<kPol>(a, rays, cnt, n_legal, e, ply, lane, ac, lp, acts);
+                                choose<kPol>(a, rays, n_legal, e, ply, lane, ac, lp, acts);
                                 act = ac;
                             }
                         }
@@ -1140,9 +1174,9 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                             if (lane == 0) fld<int32_t>(rec, R_INVALID) += 1;
                             __syncwarp();
                         } else if (chk) {
-                            enumerate(rec, rec[R_PLAYER], rays, lane, cnt);
+                            n_moves = enumerate(rec, rec[R_PLAYER], rays, lane);
                             rays_ok = true;
-                            if (count_of(cnt) == 0) {
+                            if (n_moves == 0) {
                                 if (lane == 0) {
                                     fld<int8_t>(rec, R_OUTCOME) = (int8_t)(rec[R_PLAYER] == 0 ? 1 : 0);
                                     rec[R_TERM] = 1;
@@ -1176,13 +1210,13 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                                  has(F_SAMPLE_OUT);
             int n = 0;
             if (observe) {
-                if (!rays_ok) enumerate(rec, rec[R_PLAYER], rays, lane, cnt);
-                n = count_of(cnt);
+                if (!rays_ok) n_moves = enumerate(rec, rec[R_PLAYER], rays, lane);
+                n = n_moves;
             }
             if (has(F_PROPOSE) || has(F_SAMPLE_OUT)) {
                 int ac;
                 float lp;
-                choose<kPol>(a, rays, cnt, n, e, pp, lane, ac, lp, acts, kPol == SB_POLICY_UNIFORM ? &u_prop : nullptr);
+                choose<kPol>(a, rays, n, e, pp, lane, ac, lp, acts, kPol == SB_POLICY_UNIFORM ? &u_prop : nullptr);
                 if (lane == 0) {
                     if (has(F_PROPOSE)) {
                         fld<int16_t>(rec, R_PROP) = (int16_t)ac;
