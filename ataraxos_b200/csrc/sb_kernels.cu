@@ -16,6 +16,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "sb_device.cuh"
@@ -1609,10 +1610,11 @@ struct OccEntry {
     int blocks;
 };
 std::mutex g_mu;
-OccEntry g_occ[64];
+constexpr int CACHE_N = 512;  // kernel instantiations x devices x shared-memory sizes
+OccEntry g_occ[CACHE_N];
 int g_nocc = 0;
-const void* g_attr_fn[64];
-int g_attr_dev[64];
+const void* g_attr_fn[CACHE_N];
+int g_attr_dev[CACHE_N];
 int g_nattr = 0;
 
 // Opt every env_kernel instantiation into the device's full per-block shared
@@ -1637,7 +1639,7 @@ int blocks_per_sm(const void* fn, int dev, int smem, int* out) {
         // dynamic shared memory may use what the static part leaves
         e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-        if (g_nattr < 64) {
+        if (g_nattr < CACHE_N) {
             g_attr_fn[g_nattr] = fn;
             g_attr_dev[g_nattr++] = dev;
         }
@@ -1646,21 +1648,21 @@ int blocks_per_sm(const void* fn, int dev, int smem, int* out) {
     cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, sb::WARPS * 32, smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
     if (nb < 1) return fail(SB_E_CUDA, "kernel does not fit on an SM with %d bytes of shared memory", smem);
-    if (g_nocc < 64) g_occ[g_nocc++] = OccEntry{fn, dev, smem, nb};
+    if (g_nocc < CACHE_N) g_occ[g_nocc++] = OccEntry{fn, dev, smem, nb};
     *out = nb;
     return SB_OK;
 }
 
 int sm_count(int dev, int* out) {
-    static int cache[64] = {0};
+    static std::atomic<int> cache[64];
     if (dev < 0 || dev >= 64) return fail(SB_E_ARG, "device index out of range");
-    if (!cache[dev]) {
-        int v = 0;
+    int v = cache[dev].load(std::memory_order_relaxed);
+    if (!v) {
         cudaError_t e = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
-        cache[dev] = v;
+        cache[dev].store(v, std::memory_order_relaxed);
     }
-    *out = cache[dev];
+    *out = v;
     return SB_OK;
 }
 
