@@ -96,6 +96,10 @@ class SbExport(ctypes.Structure):
     _fields_ = [(f, vp) for f in EXPORT_FIELDS]
 
 
+class SbServe(ctypes.Structure):
+    _fields_ = [("ctl", vp), ("dev", vp), ("n_ctas", ctypes.c_int64), ("limit_ns", ctypes.c_int64)]
+
+
 class SbHostIo(ctypes.Structure):
     _fields_ = [
         ("actions_host", vp),
@@ -122,6 +126,10 @@ _SIGS = {
                                ctypes.POINTER(SbStepOut), vp]),
     "sb_step_host": (ctypes.c_int, [ctypes.POINTER(SbState), ctypes.POINTER(SbHostIo), ctypes.c_int64,
                                     ctypes.POINTER(SbPolicy), ctypes.c_int, ctypes.POINTER(SbStepOut), vp]),
+    "sb_serve_start": (ctypes.c_int, [ctypes.POINTER(SbState), ctypes.c_int64, ctypes.c_int, vp,
+                                      ctypes.POINTER(SbStepOut), ctypes.POINTER(SbServe), vp]),
+    "sb_serve_step": (ctypes.c_int, [ctypes.POINTER(SbServe), ctypes.c_int64, ctypes.c_int64]),
+    "sb_serve_stop": (ctypes.c_int, [ctypes.POINTER(SbServe), ctypes.c_int64, vp]),
     "sb_rollout": (ctypes.c_int, [ctypes.POINTER(SbState), ctypes.c_int64, ctypes.POINTER(SbPolicy), ctypes.c_int,
                                   ctypes.c_int32, ctypes.POINTER(SbTraj), vp]),
     "sb_belief_resample": (ctypes.c_int, [ctypes.POINTER(SbState), ctypes.POINTER(SbState), vp, vp]),

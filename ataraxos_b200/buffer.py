@@ -652,6 +652,12 @@ class StrategoRolloutBuffer:
             }
         return self._host
 
+    def serve(self, **kw):
+        """A persistent step server over this buffer (``ataraxos_b200.serve.StepServer``)."""
+        from .serve import StepServer
+
+        return StepServer(self, **kw)
+
     def episode_stats(self) -> torch.Tensor:
         """int64 [5]: games finished in step(), red wins, blue wins, draws, Σ lengths."""
         return self._ensure_outputs()["stats"]

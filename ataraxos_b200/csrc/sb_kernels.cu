@@ -15,6 +15,7 @@
 #include <stdarg.h>
 #include <stdio.h>
 #include <string.h>
+#include <time.h>
 
 #include <atomic>
 #include <mutex>
@@ -84,7 +85,19 @@ struct KArgs {
     int64_t slot0;
     int32_t rules;  // SB_RULES_*
     uint8_t* isf;   // [n, ISF_TS_BYTES] under SB_RULES_ISF
+    // step server (MODE_SERVE): control block in mapped page-locked host
+    // memory (SERVE_GO, SERVE_STOP, SERVE_DONE), its device relay
+    // (SERVE_GO, SERVE_STOP, DEV_DONE_COUNT), the page-locked host results
+    // and the longest a CTA waits for the host's next step
+    int64_t* serve_ctl;
+    int64_t* serve_dev;
+    float* serve_reward;
+    int16_t* serve_next;
+    uint8_t* serve_done;
+    int64_t serve_limit_ns;
 };
+
+constexpr int SERVE_GO = 0, SERVE_STOP = 1, SERVE_DONE = 16, DEV_DONE_COUNT = 2;
 
 constexpr int WARPS = 8;  // warps (envs in flight) per CTA
 constexpr int ZOB_N = 2600;  // entries of the [10,10,2,13] Zobrist table
@@ -991,18 +1004,51 @@ constexpr int MODE_GENERIC = 0, MODE_STEP_UNIFORM = 1, MODE_STEP_GUMBEL = 2, MOD
 // added to a step mode: the kernel also carries the ISF repetition rules
 // (the generic kernel always does; the CUDA-rules step kernels never pay for them)
 constexpr int MODE_ISF = 8;
-// MODE_STEP_PROD is MODE_STEP_UNIFORM for a single ply with a u8 mask and /
-// or an infostate (the config-2 step).  There every env's game logic runs in
-// one wave at the same time, so HBM would idle through it: each 8-warp CTA
-// gives one warp to a producer that streams the envs' zero rows with bulk
-// copies while the other 7 play; an mbarrier orders the completed zero rows
-// before the one-hots stored on top, a second one keeps the producer at most
-// one batch ahead.  Multi-ply and Gumbel launches keep all 8 warps on envs
-// (measured faster there).
+// added to MODE_STEP_PROD: a persistent step server that runs one ply per
+// step the host publishes in mapped memory, until told to stop
+constexpr int MODE_SERVE = 16;
+
+// Step server handshake.  CTA 0 relays the host's step (polled over PCIe,
+// bounded) into device memory; every CTA's thread 0 then waits (bounded) on
+// that relay in L2, so PCIe carries one poller.  Returns 1 to run step t, 0
+// to stop (asked to, or gave up).
+__device__ int serve_wait(const KArgs& a, int64_t t) {
+    const uint64_t t0 = global_ns();
+    if (blockIdx.x == 0) {
+        for (;;) {
+            int64_t go;
+            asm volatile("ld.acquire.sys.global.s64 %0, [%1];" : "=l"(go) : "l"(a.serve_ctl + SERVE_GO) : "memory");
+            if (go >= t) {
+                int64_t stop;
+                asm volatile("ld.acquire.sys.global.s64 %0, [%1];" : "=l"(stop) : "l"(a.serve_ctl + SERVE_STOP) : "memory");
+                asm volatile("st.relaxed.gpu.global.s64 [%0], %1;" ::"l"(a.serve_dev + SERVE_STOP), "l"(stop) : "memory");
+                asm volatile("st.release.gpu.global.s64 [%0], %1;" ::"l"(a.serve_dev + SERVE_GO), "l"(t) : "memory");
+                return stop ? 0 : 1;
+            }
+            if (global_ns() - t0 > (uint64_t)a.serve_limit_ns) break;
+            __nanosleep(100);
+        }
+    } else {
+        for (;;) {
+            int64_t go;
+            asm volatile("ld.acquire.gpu.global.s64 %0, [%1];" : "=l"(go) : "l"(a.serve_dev + SERVE_GO) : "memory");
+            if (go >= t) {
+                int64_t stop;
+                asm volatile("ld.relaxed.gpu.global.s64 %0, [%1];" : "=l"(stop) : "l"(a.serve_dev + SERVE_STOP) : "memory");
+                return stop ? 0 : 1;
+            }
+            if (global_ns() - t0 > (uint64_t)a.serve_limit_ns) break;
+            __nanosleep(100);
+        }
+    }
+    if (a.status) atomicOr(a.status, SB_STATUS_WAIT_TIMEOUT);
+    return 0;
+}
 
 template <typename T, int MODE>
 __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
-    constexpr int M = MODE & ~MODE_ISF;
+    constexpr int M = MODE & ~(MODE_ISF | MODE_SERVE);
+    constexpr bool kServe = (MODE & MODE_SERVE) != 0;
     constexpr bool kStep = M != MODE_GENERIC;
     constexpr bool kProd = M == MODE_STEP_PROD;
     const bool isf_on = (M == MODE_GENERIC || (MODE & MODE_ISF) != 0) && a.rules == SB_RULES_ISF;
@@ -1068,7 +1114,24 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
     const int64_t stride = (int64_t)gridDim.x * ENVW;
     const int64_t first = (int64_t)blockIdx.x * ENVW;
     int64_t iter = 0;
-    for (int64_t base = first; base < a.n; base += stride) {
+    // step server: the CTA's actions and results, each crossing PCIe as one
+    // coalesced transfer per step
+    __shared__ int s_cmd;
+    __shared__ int64_t s_act[WARPS];
+    __shared__ float s_rew[WARPS];
+    __shared__ int16_t s_nxt[WARPS];
+    __shared__ uint8_t s_dn[WARPS];
+    for (int64_t t = 1;; ++t) {
+      if (kServe) {
+        if (threadIdx.x == 0) s_cmd = serve_wait(a, t);
+        __syncthreads();
+        if (s_cmd != 1) break;
+        if (a.actions && producer && lane < ENVW && first + lane < a.n)
+            s_act[lane] = (int64_t)__ldcv(reinterpret_cast<const long long*>(a.actions) + first + lane);
+        __syncthreads();
+      }
+      const int64_t ply_base = kServe ? a.ply + t - 1 : a.ply;
+      for (int64_t base = first; base < a.n; base += stride) {
         if (producer) {
             if (zeros) {
                 // at most one batch ahead of the slowest env warp
@@ -1111,14 +1174,14 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
         }
 
         for (int p = 0; p < np; ++p, ++iter) {
-            const int64_t ply = a.ply + p;
+            const int64_t ply = ply_base + p;
             const int64_t s_cur = (a.slot0 + p) % a.n_slots;
             const int64_t s_next = has(F_APPLY) ? (a.slot0 + p + 1) % a.n_slots : a.slot0 % a.n_slots;
             const int64_t ic = s_cur * a.n + e, in = s_next * a.n + e;
             uint8_t* ginfo = has(F_INFO) ? reinterpret_cast<uint8_t*>(a.info) + in * info_env : nullptr;
             // the uniform proposal's random word depends only on (seed, env,
             // ply): drawn first, off the game logic's critical path
-            const int64_t pp = has(F_PROPOSE) ? (has(F_APPLY) ? ply + 1 : ply) : a.ply;
+            const int64_t pp = has(F_PROPOSE) ? (has(F_APPLY) ? ply + 1 : ply) : ply_base;
             uint32_t u_prop = 0;
             if (kPol == SB_POLICY_UNIFORM)
                 u_prop = philox((uint32_t)(a.env_base + e), (uint32_t)pp, (uint32_t)((uint64_t)pp >> 32), TAG_ACTION, a.seed).x;
@@ -1137,7 +1200,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                 if (!was_term) {
                     const int pm = rec[R_PLAYER];
                     int n_legal = -1;
-                    if (a.actions) act = a.actions[e];
+                    if (a.actions) act = kServe ? s_act[w] : a.actions[e];
                     if (!a.actions || has(F_STEP)) {
                         if (fld<int32_t>(rec, R_PROPPLY) == (int32_t)ply &&
                             rec[R_PROPKIND] == (kPol >= 0 ? kPol : a.policy) && !a.logits) {
@@ -1225,7 +1288,8 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                         rec[R_PROPKIND] = (uint8_t)(kPol >= 0 ? kPol : a.policy);
                         fld<int16_t>(rec, R_NLEGAL) = (int16_t)n;
                         fld<float>(rec, R_PROPLP) = lp;
-                        if (a.next_action) a.next_action[in] = (int16_t)ac;
+                        if (kServe) s_nxt[w] = (int16_t)ac;
+                        else if (a.next_action) a.next_action[in] = (int16_t)ac;
                         if (a.next_logprob) a.next_logprob[in] = lp;
                     }
                     if (has(F_SAMPLE_OUT)) {
@@ -1239,8 +1303,14 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                 if (has(F_HAS_LEGAL)) a.has_legal[e] = n > 0;
                 if (has(F_HASH)) a.hash[in] = fld<int64_t>(rec, R_ZHASH);
                 if (tr.valid) {
-                    if (a.reward) a.reward[ic] = tr.oc == 0 ? 1.0f : (tr.oc == 1 ? -1.0f : 0.0f);
-                    if (a.done) a.done[ic] = tr.term ? 1 : 0;
+                    const float rw = tr.oc == 0 ? 1.0f : (tr.oc == 1 ? -1.0f : 0.0f);
+                    if (kServe) {
+                        s_rew[w] = rw;
+                        s_dn[w] = tr.term ? 1 : 0;
+                    } else {
+                        if (a.reward) a.reward[ic] = rw;
+                        if (a.done) a.done[ic] = tr.term ? 1 : 0;
+                    }
                     if (a.action_taken) a.action_taken[ic] = tr.act;
                     if (a.logprob_taken) a.logprob_taken[ic] = tr.lp;
                     if (a.stats && tr.ended) {
@@ -1289,6 +1359,29 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
 
         if (live && dirty) reinterpret_cast<uint2*>(a.rec + e * REC)[lane] = reinterpret_cast<const uint2*>(rec)[lane];
         __syncwarp();
+      }
+      if (!kServe) break;
+      __syncthreads();
+      // the CTA's results go to page-locked host memory in three contiguous
+      // runs, then are made visible system wide; the CTA that completes the
+      // step's count tells the host
+      if (producer) {
+          const int64_t e = first + (lane % 8);
+          if (lane < ENVW && e < a.n) a.serve_reward[e] = s_rew[lane];
+          else if (lane >= 8 && lane < 8 + ENVW && e < a.n) a.serve_next[e] = s_nxt[lane - 8];
+          else if (lane >= 16 && lane < 16 + ENVW && e < a.n) a.serve_done[e] = s_dn[lane - 16];
+          __threadfence_system();
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+          unsigned long long old;
+          asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], 1;"
+                       : "=l"(old)
+                       : "l"(a.serve_dev + DEV_DONE_COUNT)
+                       : "memory");
+          if ((int64_t)old + 1 == (int64_t)gridDim.x * t)
+              asm volatile("st.release.sys.global.s64 [%0], %1;" ::"l"(a.serve_ctl + SERVE_DONE), "l"(t) : "memory");
+      }
     }
     // the table's bulk copy must land before the CTA's shared memory goes away
     if (threadIdx.x == 0) zob_wait();
@@ -1921,6 +2014,106 @@ int sb_step_host(const sb_state* s, const sb_host_io* io, int64_t ply, const sb_
         if (e != cudaSuccess) return cuda_fail(e, "stream synchronize");
     }
     return SB_OK;
+}
+
+int sb_serve_start(const sb_state* s, int64_t ply0, int auto_reset, const int64_t* actions_host,
+                   const sb_step_out* out, sb_serve* sv, void* stream) {
+    int rc = check_state(s);
+    if (rc != SB_OK) return rc;
+    if (!sv || !sv->ctl || !sv->dev || !out) return fail(SB_E_ARG, "serve control blocks or outputs are NULL");
+    if (!aligned(sv->dev, 8)) return fail(SB_E_ARG, "serve device relay not 8-byte aligned");
+    if (s->n < 1) return fail(SB_E_ARG, "no envs");
+    if (s->rules != SB_RULES_CUDA) return fail(SB_E_ARG, "the step server runs the CUDA repetition rules");
+    if (sv->limit_ns <= 0) return fail(SB_E_ARG, "limit_ns must be > 0");
+    if (auto_reset && !s->setup_pool) return fail(SB_E_NOPOOL, "auto_reset needs a setup pool");
+    sb_step_out o = *out;
+    if (!o.infostate && !o.mask_u8) return fail(SB_E_ARG, "the step server writes an infostate and / or a u8 mask");
+    if (o.mask_bits || o.hash) return fail(SB_E_ARG, "the step server writes no bit-packed mask or hash");
+    void* d = nullptr;
+    if ((rc = device_view(sv->ctl, &d)) != SB_OK) return rc;
+    int64_t* ctl = static_cast<int64_t*>(d);
+    const int64_t* acts = nullptr;
+    if (actions_host) {
+        if ((rc = device_view(actions_host, &d)) != SB_OK) return rc;
+        acts = static_cast<const int64_t*>(d);
+    }
+    if (!o.reward || !o.done || !o.next_action) return fail(SB_E_ARG, "the step server needs reward, done, next_action");
+    if ((rc = device_view(o.reward, &d)) == SB_OK) o.reward = static_cast<float*>(d);
+    if (rc == SB_OK && (rc = device_view(o.done, &d)) == SB_OK) o.done = static_cast<uint8_t*>(d);
+    if (rc == SB_OK && (rc = device_view(o.next_action, &d)) == SB_OK) o.next_action = static_cast<int16_t*>(d);
+    if (rc != SB_OK) return rc;
+    if (o.infostate && (rc = check_info(o.infostate, o.info_dtype, o.info_layout)) != SB_OK) return rc;
+    if (o.mask_u8 && !aligned(o.mask_u8, 16)) return fail(SB_E_ARG, "mask_u8 not 16-byte aligned");
+    sb::KArgs k = base_args(s);
+    k.flags = sb::F_APPLY | sb::F_STEP | sb::F_PROPOSE | (auto_reset ? sb::F_AUTO_RESET : 0);
+    k.actions = acts;
+    k.ply = ply0;
+    k.propose_ply = ply0 + 1;
+    k.policy = SB_POLICY_UNIFORM;
+    int dtype = SB_DTYPE_F32;
+    if (o.infostate) {
+        k.flags |= sb::F_INFO;
+        k.info = o.infostate;
+        k.info_layout = o.info_layout;
+        dtype = o.info_dtype;
+    }
+    if (o.mask_u8) {
+        k.flags |= sb::F_MASK_U8;
+        k.mask_u8 = o.mask_u8;
+    }
+    k.action_taken = o.action_taken;
+    k.logprob_taken = o.logprob_taken;
+    k.next_logprob = o.next_logprob;
+    k.stats = o.stats;
+    k.serve_ctl = ctl;
+    k.serve_dev = sv->dev;
+    k.serve_reward = o.reward;
+    k.serve_next = o.next_action;
+    k.serve_done = o.done;
+    k.serve_limit_ns = sv->limit_ns;
+    plan_smem(k);
+    constexpr int SV = sb::MODE_STEP_PROD | sb::MODE_SERVE;
+    const void* fn = dtype == SB_DTYPE_F32 ? (const void*)sb::env_kernel<float, SV> : (const void*)sb::env_kernel<uint16_t, SV>;
+    int dev = 0, nb = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    const int smem = sb::ZERO_BYTES + sb::WARPS * k.sm_warp;
+    if ((rc = blocks_per_sm(fn, dev, smem, &nb)) != SB_OK) return rc;
+    if ((rc = sm_count(dev, &sms)) != SB_OK) return rc;
+    const int64_t blocks = (s->n + sb::WARPS - 2) / (sb::WARPS - 1);
+    if (blocks > (int64_t)sms * nb)
+        return fail(SB_E_ARG, "%lld envs need %lld resident CTAs; this GPU holds %lld", (long long)s->n,
+                    (long long)blocks, (long long)sms * nb);
+    memset(sv->ctl, 0, 17 * sizeof(int64_t));
+    e = cudaMemsetAsync(sv->dev, 0, 4 * sizeof(int64_t), (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+    sv->n_ctas = blocks;
+    void* args[] = {&k};
+    // cooperative: every CTA resident at once (the host waits for all of them)
+    e = cudaLaunchCooperativeKernel(fn, dim3((unsigned)blocks), dim3(sb::WARPS * 32), args, (size_t)smem,
+                                    (cudaStream_t)stream);
+    return e == cudaSuccess ? SB_OK : cuda_fail(e, "step server launch");
+}
+
+int sb_serve_step(const sb_serve* sv, int64_t t, int64_t timeout_ns) {
+    if (!sv || !sv->ctl || sv->n_ctas < 1) return fail(SB_E_ARG, "no running step server");
+    __atomic_store_n(sv->ctl + sb::SERVE_GO, t, __ATOMIC_RELEASE);
+    timespec t0, now;
+    clock_gettime(CLOCK_MONOTONIC, &t0);
+    while (__atomic_load_n(sv->ctl + sb::SERVE_DONE, __ATOMIC_ACQUIRE) < t) {
+        clock_gettime(CLOCK_MONOTONIC, &now);
+        const int64_t dt = (int64_t)(now.tv_sec - t0.tv_sec) * 1000000000ll + (now.tv_nsec - t0.tv_nsec);
+        if (dt > timeout_ns) return fail(SB_E_CUDA, "step %lld not finished in time", (long long)t);
+    }
+    return SB_OK;
+}
+
+int sb_serve_stop(const sb_serve* sv, int64_t t_done, void* stream) {
+    if (!sv || !sv->ctl) return fail(SB_E_ARG, "no step server");
+    __atomic_store_n(sv->ctl + sb::SERVE_STOP, (int64_t)1, __ATOMIC_RELEASE);
+    __atomic_store_n(sv->ctl + sb::SERVE_GO, t_done + 1, __ATOMIC_RELEASE);
+    cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+    return e == cudaSuccess ? SB_OK : cuda_fail(e, "step server stop");
 }
 
 int sb_rollout(const sb_state* s, int64_t ply, const sb_policy* policy, int auto_reset, int32_t n_plies,

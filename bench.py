@@ -267,32 +267,48 @@ def timed_launches(ctx: Ctx, launch, k: int, flush_mib: int):
 
 
 def e2e_loop(ctx: Ctx, buf, steps: int, policy: str = "uniform", total_envs: int | None = None
-             ) -> tuple[float, int, int]:
-    """The public host-side API, ``StrategoRolloutBuffer.step_host``: per step the
-    actions (int64[B], page-locked host memory) cross to the device, the fused
-    step runs, and reward, done and the next proposed actions cross back into
-    page-locked host memory; the call returns once they have landed.  The
-    default transfer is in place (the kernel reads the actions from, and writes
-    the results to, mapped host memory over PCIe: no copy-engine transfers).
-    The host takes the proposals as its next actions.  Returns (updates/s,
-    h2d, d2h bytes)."""
+             ) -> tuple[float, int, int, str]:
+    """The public host-side API with host buffers: per step the actions
+    (int64[B], page-locked host memory) cross to the device, the fused step
+    runs, and reward, done and the next proposed actions cross back into
+    page-locked host memory; the host takes the proposals as its next actions.
+    Uniform steps go through the persistent step server
+    (``StrategoRolloutBuffer.serve``: no launch or stream synchronisation per
+    step, CUDA events around the server kernel's whole life); otherwise
+    ``step_host`` (the kernel reads / writes the page-locked memory in place,
+    CUDA events around the loop).  Returns (updates/s, h2d, d2h bytes, api)."""
+    from ataraxos_b200.serve import StepServer
+
     B = buf.n_games
-    h_act = torch.empty(B, dtype=torch.int64, pin_memory=True)
+    total = ctx.world * B if total_envs is None else total_envs
     r = buf.step_host(None, policy=policy)
     ctx.barrier()
     torch.cuda.synchronize(ctx.dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(ctx.stream)
-    for _ in range(steps):
-        h_act.copy_(r.next_action)
-        r = buf.step_host(h_act, policy=policy)
-    e1.record(ctx.stream)
+    if ctx.args.e2e_api == "serve" and policy == "uniform" and B <= StepServer.max_envs(buf.device):
+        st = torch.cuda.Stream(ctx.dev)
+        e0.record(st)
+        with StepServer(buf, stream=st) as srv:
+            acts = srv.actions
+            acts.copy_(r.next_action)
+            for _ in range(steps):
+                r = srv.step(acts)
+                acts.copy_(r.next_action)
+        e1.record(st)
+        api = "StrategoRolloutBuffer.serve().step (persistent step server)"
+    else:
+        h_act = torch.empty(B, dtype=torch.int64, pin_memory=True)
+        e0.record(ctx.stream)
+        for _ in range(steps):
+            h_act.copy_(r.next_action)
+            r = buf.step_host(h_act, policy=policy)
+        e1.record(ctx.stream)
+        api = "StrategoRolloutBuffer.step_host"
     torch.cuda.synchronize(ctx.dev)
     ctx.barrier()
     ms = ctx.max_over_ranks(e0.elapsed_time(e1))
-    total = ctx.world * B if total_envs is None else total_envs
     return total * steps / (ms / 1e3), B * 8, int(r.reward.numel() * 4 + r.next_action.numel() * 2
-                                                            + r.done.numel())
+                                                  + r.done.numel()), api
 
 
 def run_step_config(ctx: Ctx, cfg: int) -> dict:
@@ -317,14 +333,14 @@ def run_step_config(ctx: Ctx, cfg: int) -> dict:
     launch_ms = total_ms / a.steps
     stats = ctx.gather_stats(buf.episode_stats().clone())
     if cfg == 2:
-        e2e, h2d, d2h = e2e_loop(ctx, buf, a.e2e_steps)
+        e2e, h2d, d2h, api = e2e_loop(ctx, buf, a.e2e_steps)
         workload = (f"config2: {B} envs/GPU, seeded random setups (pool {pool}), uniform random legal actions, "
                     "auto-reset, bf16 [B,488,10,10] infostate (75 live planes rewritten per ply), u8 [B,100,100] "
                     "mask; one step = one fused-kernel ply over all envs")
         l2 = f"flushed between timed steps ({a.flush_mib} MiB write, then {a.flush_mib // 2} MiB read)"
         scaling = "weak"
     else:
-        e2e, h2d, d2h = e2e_loop(ctx, buf, max(10, a.e2e_steps // 10), policy, total)
+        e2e, h2d, d2h, api = e2e_loop(ctx, buf, max(10, a.e2e_steps // 10), policy, total)
         workload = (f"config3: {total} envs split over {ctx.world} GPU(s) ({B}/GPU), actions by Gumbel-max "
                     "over virtual Philox N(0,1) logits of the legal moves (logits never materialised), setups from "
                     f"a {pool}-entry pool, auto-reset, bf16 dense infostate + u8 mask")
@@ -335,7 +351,7 @@ def run_step_config(ctx: Ctx, cfg: int) -> dict:
         "launch_ms": launch_ms,
         "envs_per_launch": B, "plies_per_launch": 1, "bytes_per_update": BYTES_PER_UPDATE, "clocks": clocks,
         "stats": stats, "e2e": {"value": e2e, "unit": "updates/s", "h2d_bytes_per_step": h2d,
-                                "d2h_bytes_per_step": d2h},
+                                "d2h_bytes_per_step": d2h, "api": api},
         "gpu_launches": a.steps, "config": {"workload": workload, "envs_per_gpu": B, "l2": l2,
                                             "parallelism": f"env-sharded x{ctx.world}, no step-path collective"},
         "scaling": scaling, "traffic": _profile_traffic("step_kernel_config2.txt") if cfg == 2 else None,
@@ -458,6 +474,8 @@ def main() -> None:
     ap.add_argument("--envs", type=int, default=4096, help="envs per GPU (config 2)")
     ap.add_argument("--plies-per-launch", type=int, default=8, help="config 4 rollout launch length")
     ap.add_argument("--e2e-steps", type=int, default=500)
+    ap.add_argument("--e2e-api", choices=["serve", "step_host"], default="step_host",
+                    help="host API of the e2e loop: the persistent step server or step_host")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--flush-mib", type=int, default=512)
     args = ap.parse_args()

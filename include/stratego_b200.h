@@ -181,6 +181,32 @@ typedef struct sb_host_io {
 int sb_step_host(const sb_state *s, const sb_host_io *io, int64_t ply, const sb_policy *policy, int auto_reset,
                  const sb_step_out *out, void *stream);
 
+/* ---- step server ----------------------------------------------------------
+ * north-star: a persistent kernel that plays one fused ply (as sb_step with
+ * the uniform policy, auto-reset and dense outputs) each time the host
+ * publishes a step in a control block of mapped page-locked memory, so a
+ * host-driven loop pays no kernel launch and no stream synchronisation per
+ * ply.  Actions (or NULL: the cached proposals) are read from, and reward /
+ * done / next_action written to, mapped page-locked host memory; infostate
+ * and mask go to device memory.  Every CTA gives up after limit_ns without a
+ * step (status SB_STATUS_WAIT_TIMEOUT) and the kernel ends; nothing else may
+ * use the state while the server runs.  At most (SMs x resident CTAs x 7)
+ * envs (4,144 on a B200): all CTAs must be resident together. */
+typedef struct sb_serve {
+    int64_t *ctl;        /* mapped page-locked int64[17], zeroed by sb_serve_start: [0] step
+                            published by the host, [1] stop, [16] last step every CTA finished */
+    int64_t *dev;        /* device int64[4]: the kernel's relay of ctl (one CTA polls the host) */
+    int64_t n_ctas;      /* set by sb_serve_start */
+    int64_t limit_ns;    /* longest a CTA waits for the next step (e.g. 2e9) */
+} sb_serve;
+
+int sb_serve_start(const sb_state *s, int64_t ply0, int auto_reset, const int64_t *actions_host,
+                   const sb_step_out *out, sb_serve *sv, void *stream);
+/* publish step t (1, 2, ...) and wait, at most timeout_ns, until every CTA has finished it */
+int sb_serve_step(const sb_serve *sv, int64_t t, int64_t timeout_ns);
+/* ask the kernel to stop after step t_done and wait for it on `stream` */
+int sb_serve_stop(const sb_serve *sv, int64_t t_done, void *stream);
+
 /* north-star: a trajectory ring of n_slots slots; every array is laid out
  * [n_slots, n, ...] and any pointer may be NULL. */
 typedef struct sb_traj {
