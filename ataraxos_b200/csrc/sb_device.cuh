@@ -197,15 +197,6 @@ __device__ __forceinline__ void bulk_g2s(void* sdst, const void* gsrc, uint32_t 
                  : "memory");
 }
 
-// Named CTA barriers (ids 1-15; 0 is __syncthreads): sync waits, arrive
-// only counts in; nthreads is the total of both sides, a multiple of 32.
-__device__ __forceinline__ void named_sync(int id, int nthreads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
-__device__ __forceinline__ void named_arrive(int id, int nthreads) {
-    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
-
 // Three bits of a Zobrist hash in a 64-bit Bloom filter (the hash bits are
 // uniformly random, so its low 18 bits serve as three independent indices).
 __device__ __forceinline__ uint64_t bloom_bits(uint64_t h) {

@@ -772,11 +772,6 @@ struct InfoGeom {
     static constexpr int HB = 32 * PB;                        // channels 456-487
 };
 
-__device__ __forceinline__ void zero_chunks(uint8_t* g, int nchunks, int lane) {
-    const uint4 Z = make_uint4(0, 0, 0, 0);
-    for (int i = lane; i < nchunks; i += 32) st16(g + i * 16, Z);
-}
-
 // Four consecutive elements of one plane row (one lane's squares 4L..4L+3):
 // two words of bf16 bits or four words of f32 bits.
 template <typename T>

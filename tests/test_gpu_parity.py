@@ -365,3 +365,42 @@ def test_bad_inputs_raise():
         b.reset_all(torch.zeros((2, 10, 9), dtype=torch.int8), torch.zeros((2, 10, 10), dtype=torch.int8))
     with pytest.raises(RuntimeError):
         b.step(None)  # auto_reset without a setup pool
+
+
+def test_empty_buffer():
+    b = _buf(0, pool_size=16)
+    b.reset_all_from_pool()
+    out = b.step(None)
+    assert out.infostate.shape == (0, 488, 10, 10) and out.legal_mask.shape == (0, 100, 100)
+    assert b.compute_legal_action_mask().shape == (0, 100, 100)
+    assert b.compute_infostate_tensor().shape == (0, 488, 10, 10)
+    assert b.hash_board().shape == (0,)
+    r = b.step_host(None)
+    assert r.reward.shape == (0,)
+    assert b.current_step() == 0
+
+
+def test_full_size_config3_properties_and_subsample_parity():
+    """Benchmark config 3 at full size on one GPU (262,144 envs, Gumbel): every
+    proposed move is set in its game's legal mask, and a subsample of 257
+    games, rebuilt on the oracle from the exported state, has bit-identical
+    masks and bfloat16 infostates."""
+    n = 262144
+    b = _buf(n, seed=3, pool_size=1 << 20)
+    b.reset_all_from_pool()
+    for _ in range(3):
+        out = b.step(None, policy="gumbel")
+    nxt = out.next_action.long()
+    flat = out.legal_mask.view(n, -1)
+    live = nxt >= 0
+    assert int(live.sum()) == n
+    assert bool(flat.gather(1, nxt.clamp(min=0)[:, None]).squeeze(1)[live].all())
+    idx = torch.arange(0, n, 1021, device="cuda")
+    st = export_np(b)
+    sub = idx.cpu().numpy()
+    o = oracle.OracleState(len(sub))
+    for k, v in o.a.items():
+        np.copyto(v, st[k][sub].astype(v.dtype).reshape(v.shape))
+    np.testing.assert_array_equal(flat[idx].cpu().numpy().reshape(-1, 100, 100).view(np.uint8), o.legal_mask_u8())
+    bits = out.infostate[idx].view(torch.int16).cpu().numpy().view(np.uint16)
+    np.testing.assert_array_equal(bits, o.infostate_bf16_bits())
