@@ -97,7 +97,8 @@ class SbExport(ctypes.Structure):
 
 
 class SbServe(ctypes.Structure):
-    _fields_ = [("ctl", vp), ("dev", vp), ("n_ctas", ctypes.c_int64), ("limit_ns", ctypes.c_int64)]
+    _fields_ = [("ctl", vp), ("dev", vp), ("back_dev", vp), ("back_host", vp), ("back_bytes", ctypes.c_int64),
+                ("n_ctas", ctypes.c_int64), ("limit_ns", ctypes.c_int64)]
 
 
 class SbHostIo(ctypes.Structure):

@@ -87,13 +87,14 @@ struct KArgs {
     uint8_t* isf;   // [n, ISF_TS_BYTES] under SB_RULES_ISF
     // step server (MODE_SERVE): control block in mapped page-locked host
     // memory (SERVE_GO, SERVE_STOP, SERVE_DONE), its device relay
-    // (SERVE_GO, SERVE_STOP, DEV_DONE_COUNT), the page-locked host results
-    // and the longest a CTA waits for the host's next step
+    // (SERVE_GO, SERVE_STOP, DEV_DONE_COUNT), the device result block copied
+    // to page-locked host memory after every step, and the longest a CTA
+    // waits for the host's next step
     int64_t* serve_ctl;
     int64_t* serve_dev;
-    float* serve_reward;
-    int16_t* serve_next;
-    uint8_t* serve_done;
+    const uint8_t* serve_back_dev;
+    uint8_t* serve_back_host;
+    int64_t serve_back_bytes;
     int64_t serve_limit_ns;
 };
 
@@ -1109,13 +1110,10 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
     const int64_t stride = (int64_t)gridDim.x * ENVW;
     const int64_t first = (int64_t)blockIdx.x * ENVW;
     int64_t iter = 0;
-    // step server: the CTA's actions and results, each crossing PCIe as one
-    // coalesced transfer per step
-    __shared__ int s_cmd;
+    // step server: the CTA's actions cross PCIe as one coalesced read; the
+    // step's results go back as one copy by the CTA that completes the step
+    __shared__ int s_cmd, s_last;
     __shared__ int64_t s_act[WARPS];
-    __shared__ float s_rew[WARPS];
-    __shared__ int16_t s_nxt[WARPS];
-    __shared__ uint8_t s_dn[WARPS];
     for (int64_t t = 1;; ++t) {
       if (kServe) {
         if (threadIdx.x == 0) s_cmd = serve_wait(a, t);
@@ -1283,8 +1281,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                         rec[R_PROPKIND] = (uint8_t)(kPol >= 0 ? kPol : a.policy);
                         fld<int16_t>(rec, R_NLEGAL) = (int16_t)n;
                         fld<float>(rec, R_PROPLP) = lp;
-                        if (kServe) s_nxt[w] = (int16_t)ac;
-                        else if (a.next_action) a.next_action[in] = (int16_t)ac;
+                        if (a.next_action) a.next_action[in] = (int16_t)ac;
                         if (a.next_logprob) a.next_logprob[in] = lp;
                     }
                     if (has(F_SAMPLE_OUT)) {
@@ -1298,14 +1295,8 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                 if (has(F_HAS_LEGAL)) a.has_legal[e] = n > 0;
                 if (has(F_HASH)) a.hash[in] = fld<int64_t>(rec, R_ZHASH);
                 if (tr.valid) {
-                    const float rw = tr.oc == 0 ? 1.0f : (tr.oc == 1 ? -1.0f : 0.0f);
-                    if (kServe) {
-                        s_rew[w] = rw;
-                        s_dn[w] = tr.term ? 1 : 0;
-                    } else {
-                        if (a.reward) a.reward[ic] = rw;
-                        if (a.done) a.done[ic] = tr.term ? 1 : 0;
-                    }
+                    if (a.reward) a.reward[ic] = tr.oc == 0 ? 1.0f : (tr.oc == 1 ? -1.0f : 0.0f);
+                    if (a.done) a.done[ic] = tr.term ? 1 : 0;
                     if (a.action_taken) a.action_taken[ic] = tr.act;
                     if (a.logprob_taken) a.logprob_taken[ic] = tr.lp;
                     if (a.stats && tr.ended) {
@@ -1356,17 +1347,8 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
         __syncwarp();
       }
       if (!kServe) break;
-      __syncthreads();
-      // the CTA's results go to page-locked host memory in three contiguous
-      // runs, then are made visible system wide; the CTA that completes the
-      // step's count tells the host
-      if (producer) {
-          const int64_t e = first + (lane % 8);
-          if (lane < ENVW && e < a.n) a.serve_reward[e] = s_rew[lane];
-          else if (lane >= 8 && lane < 8 + ENVW && e < a.n) a.serve_next[e] = s_nxt[lane - 8];
-          else if (lane >= 16 && lane < 16 + ENVW && e < a.n) a.serve_done[e] = s_dn[lane - 16];
-          __threadfence_system();
-      }
+      // count the CTA in; the one that completes the step copies the result
+      // block to page-locked host memory and tells the host
       __syncthreads();
       if (threadIdx.x == 0) {
           unsigned long long old;
@@ -1374,9 +1356,18 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                        : "=l"(old)
                        : "l"(a.serve_dev + DEV_DONE_COUNT)
                        : "memory");
-          if ((int64_t)old + 1 == (int64_t)gridDim.x * t)
-              asm volatile("st.release.sys.global.s64 [%0], %1;" ::"l"(a.serve_ctl + SERVE_DONE), "l"(t) : "memory");
+          s_last = (int64_t)old + 1 == (int64_t)gridDim.x * t;
       }
+      __syncthreads();
+      if (s_last) {
+          const uint4* src = reinterpret_cast<const uint4*>(a.serve_back_dev);
+          uint4* dst = reinterpret_cast<uint4*>(a.serve_back_host);
+          for (int64_t i = threadIdx.x; i < a.serve_back_bytes / 16; i += blockDim.x) dst[i] = __ldcg(src + i);
+          __threadfence_system();
+      }
+      __syncthreads();
+      if (threadIdx.x == 0 && s_last)
+          asm volatile("st.release.sys.global.s64 [%0], %1;" ::"l"(a.serve_ctl + SERVE_DONE), "l"(t) : "memory");
     }
     // the table's bulk copy must land before the CTA's shared memory goes away
     if (threadIdx.x == 0) zob_wait();
@@ -2032,11 +2023,11 @@ int sb_serve_start(const sb_state* s, int64_t ply0, int auto_reset, const int64_
         if ((rc = device_view(actions_host, &d)) != SB_OK) return rc;
         acts = static_cast<const int64_t*>(d);
     }
-    if (!o.reward || !o.done || !o.next_action) return fail(SB_E_ARG, "the step server needs reward, done, next_action");
-    if ((rc = device_view(o.reward, &d)) == SB_OK) o.reward = static_cast<float*>(d);
-    if (rc == SB_OK && (rc = device_view(o.done, &d)) == SB_OK) o.done = static_cast<uint8_t*>(d);
-    if (rc == SB_OK && (rc = device_view(o.next_action, &d)) == SB_OK) o.next_action = static_cast<int16_t*>(d);
-    if (rc != SB_OK) return rc;
+    if (sv->back_bytes < 0 || sv->back_bytes % 16 || (sv->back_bytes && (!sv->back_dev || !sv->back_host)) ||
+        !aligned(sv->back_dev, 16) || !aligned(sv->back_host, 16))
+        return fail(SB_E_ARG, "bad copy-back range (16-byte aligned, a multiple of 16 bytes)");
+    void* back_host = nullptr;
+    if (sv->back_bytes && (rc = device_view(sv->back_host, &back_host)) != SB_OK) return rc;
     if (o.infostate && (rc = check_info(o.infostate, o.info_dtype, o.info_layout)) != SB_OK) return rc;
     if (o.mask_u8 && !aligned(o.mask_u8, 16)) return fail(SB_E_ARG, "mask_u8 not 16-byte aligned");
     sb::KArgs k = base_args(s);
@@ -2062,9 +2053,12 @@ int sb_serve_start(const sb_state* s, int64_t ply0, int auto_reset, const int64_
     k.stats = o.stats;
     k.serve_ctl = ctl;
     k.serve_dev = sv->dev;
-    k.serve_reward = o.reward;
-    k.serve_next = o.next_action;
-    k.serve_done = o.done;
+    k.reward = o.reward;
+    k.done = o.done;
+    k.next_action = o.next_action;
+    k.serve_back_dev = static_cast<const uint8_t*>(sv->back_dev);
+    k.serve_back_host = static_cast<uint8_t*>(back_host);
+    k.serve_back_bytes = sv->back_bytes;
     k.serve_limit_ns = sv->limit_ns;
     plan_smem(k);
     constexpr int SV = sb::MODE_STEP_PROD | sb::MODE_SERVE;

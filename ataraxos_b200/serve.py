@@ -5,10 +5,10 @@ launch or a stream synchronisation per ply.
 plays a ply of every game each time ``step()`` publishes one in a control
 block of mapped page-locked host memory: it reads that step's actions from
 page-locked host memory (or plays the cached device proposals when the step
-has none), applies them with auto-reset, writes the new infostate / u8 mask
-to the buffer's device outputs and reward / done / next action straight into
-page-locked host memory, and reports the step done per CTA.  ``step()`` returns
-once every CTA has.  The kernel ends on ``close()`` (or when no step comes for
+has none), applies them with auto-reset and writes every output to the
+buffer's device outputs; the CTA that completes the step copies the result
+block (reward / next action / done) into page-locked host memory and tells
+the host.  ``step()`` returns then.  The kernel ends on ``close()`` (or when no step comes for
 ``limit_s``).  While it runs, nothing else may use the buffer, and other
 kernels on the GPU wait for free SMs (the server keeps every CTA resident);
 it runs on a stream of its own (``stream``).
@@ -25,7 +25,7 @@ import ctypes
 import torch
 
 from . import _capi as C
-from .buffer import HostStepOutput, StepOutput, _results_layout, _results_view, _vp
+from .buffer import HostStepOutput, _results_layout, _results_view, _vp
 
 TIMEOUT_NS = 10_000_000_000  # the host's wait for one step
 
@@ -48,19 +48,15 @@ class StepServer:
         self._host_actions = bool(host_actions)
         self._ctl = torch.zeros(17, dtype=torch.int64, pin_memory=True)
         self._dev = torch.zeros(4, dtype=torch.int64, device=buf.device)
-        self._sv = C.SbServe(ctl=self._ctl.data_ptr(), dev=self._dev.data_ptr(), n_ctas=0,
+        # the device results block (reward | next_action | done) is copied
+        # whole into the page-locked block of the same layout after each step
+        self._sv = C.SbServe(ctl=self._ctl.data_ptr(), dev=self._dev.data_ptr(), back_dev=o["results"].data_ptr(),
+                             back_host=self._back.data_ptr(), back_bytes=lay["bytes"], n_ctas=0,
                              limit_ns=int(limit_s * 1e9))
-        out = buf._step_out(o, True)
-        out.reward = _results_view(self._back, lay, "reward", n).data_ptr()
-        out.next_action = _results_view(self._back, lay, "next_action", n).data_ptr()
-        out.done = _results_view(self._back, lay, "done", n).data_ptr()
-        self._out = out
+        self._out = buf._step_out(o, True)
         host = {f: _results_view(self._back, lay, f, n) for f in ("reward", "next_action", "done")}
-        dv = buf._step_views(o, True)
-        dv = StepOutput(**{**dv.__dict__, "reward": host["reward"], "done": host["done"].view(torch.bool),
-                           "next_action": host["next_action"]})
         self._ret = HostStepOutput(reward=host["reward"], done=host["done"].view(torch.bool),
-                                   next_action=host["next_action"], device=dv)
+                                   next_action=host["next_action"], device=buf._step_views(o, True))
         self._t = 0
         self._ply0 = buf.ply
         self._open = False

@@ -186,9 +186,10 @@ int sb_step_host(const sb_state *s, const sb_host_io *io, int64_t ply, const sb_
  * the uniform policy, auto-reset and dense outputs) each time the host
  * publishes a step in a control block of mapped page-locked memory, so a
  * host-driven loop pays no kernel launch and no stream synchronisation per
- * ply.  Actions (or NULL: the cached proposals) are read from, and reward /
- * done / next_action written to, mapped page-locked host memory; infostate
- * and mask go to device memory.  Every CTA gives up after limit_ns without a
+ * ply.  Actions (or NULL: the cached proposals) are read from mapped
+ * page-locked host memory; every output goes to device memory as in sb_step,
+ * and after each step the CTA that completes it copies back_dev to the
+ * mapped page-locked back_host before telling the host.  Every CTA gives up after limit_ns without a
  * step (status SB_STATUS_WAIT_TIMEOUT) and the kernel ends; nothing else may
  * use the state while the server runs.  At most (SMs x resident CTAs x 7)
  * envs (4,144 on a B200): all CTAs must be resident together. */
@@ -196,6 +197,9 @@ typedef struct sb_serve {
     int64_t *ctl;        /* mapped page-locked int64[17], zeroed by sb_serve_start: [0] step
                             published by the host, [1] stop, [16] last step every CTA finished */
     int64_t *dev;        /* device int64[4]: the kernel's relay of ctl (one CTA polls the host) */
+    const void *back_dev;/* device range copied to back_host after every step, e.g. the out */
+    void *back_host;     /*   fields reward / next_action / done laid out contiguously; mapped */
+    int64_t back_bytes;  /*   page-locked; 16-byte aligned, a multiple of 16 bytes */
     int64_t n_ctas;      /* set by sb_serve_start */
     int64_t limit_ns;    /* longest a CTA waits for the next step (e.g. 2e9) */
 } sb_serve;
