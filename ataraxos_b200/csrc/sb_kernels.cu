@@ -1,13 +1,15 @@
 // sb_kernels.cu -- B200 kernels and C ABI of the Stratego rollout simulator.
 //
-// The hot path is env_kernel<T>: one warp per env, one launch per ply, doing
-// (optionally) action sampling, move validation / combat / trackers /
-// terminal check, auto-reset from the setup pool, and the observation
-// outputs of the new state (legal mask, 488-channel infostate) in a single
-// pass over the env's 256-byte record.  Observations are staged in shared
-// memory and leave the SM as bulk asynchronous copies
-// (cp.async.bulk.global.shared::cta, the TMA engine, no multicast), so that
-// HBM sees long contiguous writes while the warp moves on.
+// The hot path is env_kernel<T, MODE>: one warp per env, one launch per ply
+// (or k plies per launch for the trajectory ring), doing action sampling,
+// move validation / combat / trackers / terminal check, auto-reset from the
+// setup pool, and the observation outputs of the new state (legal mask,
+// 488-channel infostate) in a single pass over the env's 256-byte record
+// staged in shared memory.  Dense output rows are stored straight from
+// registers as whole rows; in the single-ply production step a producer warp
+// per CTA streams the zero rows with bulk asynchronous copies
+// (cp.async.bulk.global.shared::cta, the TMA engine, no multicast) while the
+// other warps play, and the one-hots land on top after an mbarrier handshake.
 //
 // Semantics follow the reference simulator csrc/stratego_buffer.cu (cited per
 // function) with the Zobrist hash kept incrementally in the record instead of

@@ -21,9 +21,15 @@ sides; max over ranks.  Multi-GPU (torchrun): each rank owns its own 4096 envs
 scaling); an NCCL all-gather of the episode statistics follows the timed
 region.
 
+e2e: the same steps through the public host API (``step_host``: int64 actions
+from page-locked host memory in, reward / done / next action back into
+page-locked memory, the call returning when they have landed), CUDA events
+around the loop; ``--e2e-api serve`` uses the persistent step server instead.
+
 ``--impl reference`` times the reference algorithm's CPU implementation on the
 host cores: the C restatement in oracle/ (the reference's own code is Python
-and cannot run on the GPU box), same config, a bounded sample of envs per step.
+and cannot run on the GPU box), same config (the 4096-game batch per step),
+all host threads; under torchrun rank 0 alone runs it.
 """
 
 from __future__ import annotations
