@@ -16,6 +16,7 @@ SB_DTYPE_F32, SB_DTYPE_BF16 = 0, 1
 SB_LAYOUT_DENSE_ALL, SB_LAYOUT_DENSE_LIVE, SB_LAYOUT_COMPACT = 0, 1, 2
 SB_POLICY_UNIFORM, SB_POLICY_GUMBEL = 0, 1
 SB_RULES_CUDA, SB_RULES_ISF = 0, 1
+SB_NOALLOC_MAX_ENVS = 262144
 SB_STATUS_BAD_SETUP = 1
 SB_STATUS_WAIT_TIMEOUT = 2
 RECORD_BYTES = 256
@@ -127,6 +128,8 @@ _SIGS = {
                                ctypes.POINTER(SbStepOut), vp]),
     "sb_step_host": (ctypes.c_int, [ctypes.POINTER(SbState), ctypes.POINTER(SbHostIo), ctypes.c_int64,
                                     ctypes.POINTER(SbPolicy), ctypes.c_int, ctypes.POINTER(SbStepOut), vp]),
+    "sb_step_host_noalloc": (ctypes.c_int, [ctypes.POINTER(SbState), ctypes.POINTER(SbHostIo), ctypes.c_int64,
+                                            ctypes.POINTER(SbPolicy), ctypes.c_int, ctypes.POINTER(SbStepOut), vp]),
     "sb_serve_start": (ctypes.c_int, [ctypes.POINTER(SbState), ctypes.c_int64, ctypes.c_int, vp,
                                       ctypes.POINTER(SbStepOut), ctypes.POINTER(SbServe), vp]),
     "sb_serve_step": (ctypes.c_int, [ctypes.POINTER(SbServe), ctypes.c_int64, ctypes.c_int64]),

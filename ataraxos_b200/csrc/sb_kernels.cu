@@ -1623,6 +1623,11 @@ __global__ void sum_move_kernel(const uint8_t* rec, int64_t n, int64_t* out) {
 // Host side: argument checks, launch configuration, C ABI
 // ===========================================================================
 
+// Staging array of sb_step_host_noalloc: the host actions are copied here,
+// so its callers need not allocate device memory.  Host code must not use
+// the symbol as a device address; it asks for the address once per device.
+static __device__ __align__(256) int64_t g_noalloc_actions[SB_NOALLOC_MAX_ENVS];
+
 namespace {
 
 thread_local char g_err[512] = "";
@@ -1822,6 +1827,26 @@ int check_policy(const sb_policy* pol) {
     return SB_OK;
 }
 
+// Device address of g_noalloc_actions on the current device, looked up on
+// the first call per device.
+std::mutex g_noalloc_mu;
+int64_t* g_noalloc_addr[64];
+int noalloc_staging(int64_t** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return fail(SB_E_ARG, "device index out of range");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_actions);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress of the staging array");
+        g_noalloc_addr[dev] = static_cast<int64_t*>(p);
+    }
+    *out = g_noalloc_addr[dev];
+    return SB_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -2002,6 +2027,19 @@ int sb_step_host(const sb_state* s, const sb_host_io* io, int64_t ply, const sb_
         if (e != cudaSuccess) return cuda_fail(e, "stream synchronize");
     }
     return SB_OK;
+}
+
+int sb_step_host_noalloc(const sb_state* s, const sb_host_io* io, int64_t ply, const sb_policy* policy,
+                         int auto_reset, const sb_step_out* out, void* stream) {
+    int rc = check_state(s);
+    if (rc != SB_OK) return rc;
+    if (!io) return fail(SB_E_ARG, "io is NULL");
+    if (io->actions_dev) return fail(SB_E_ARG, "actions_dev must be NULL: the library stages the actions itself");
+    if (s->n > SB_NOALLOC_MAX_ENVS)
+        return fail(SB_E_ARG, "%lld envs: at most %d per call without allocation", (long long)s->n, SB_NOALLOC_MAX_ENVS);
+    sb_host_io local = *io;
+    if (io->actions_host && (rc = noalloc_staging(&local.actions_dev)) != SB_OK) return rc;
+    return sb_step_host(s, &local, ply, policy, auto_reset, out, stream);
 }
 
 int sb_serve_start(const sb_state* s, int64_t ply0, int auto_reset, const int64_t* actions_host,

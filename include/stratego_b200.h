@@ -181,6 +181,26 @@ typedef struct sb_host_io {
 int sb_step_host(const sb_state *s, const sb_host_io *io, int64_t ply, const sb_policy *policy, int auto_reset,
                  const sb_step_out *out, void *stream);
 
+/* No counterpart in the reference.  sb_step_host for callers that cannot
+ * allocate device memory for the staging copy of their host actions: code
+ * running inside another framework's fixed memory plan, which hands this
+ * library only the state and output buffers it planned, or a latency-bound
+ * loop that must not call cudaMalloc (it can synchronise the device).  The
+ * host actions are copied into a staging array built into the library (a
+ * file-scope device array of SB_NOALLOC_MAX_ENVS int64 entries, 2 MiB, held
+ * by every GPU that loads the library until the process exits); pageable or
+ * page-locked host memory both work.  io->actions_dev must be NULL; every
+ * other io field means what it does for sb_step_host.  Calls with more than
+ * SB_NOALLOC_MAX_ENVS envs return SB_E_ARG.  The first call on a device looks
+ * up the array's device address (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture.  Every call on a
+ * device shares the one array: calls that overlap on the GPU (on different
+ * streams) race on it.  Each call overwrites the entries it reads, so nothing
+ * needs clearing between calls.  Nothing is allocated. */
+#define SB_NOALLOC_MAX_ENVS 262144
+int sb_step_host_noalloc(const sb_state *s, const sb_host_io *io, int64_t ply, const sb_policy *policy,
+                         int auto_reset, const sb_step_out *out, void *stream);
+
 /* ---- step server ----------------------------------------------------------
  * north-star: a persistent kernel that plays one fused ply (as sb_step with
  * the uniform policy, auto-reset and dense outputs) each time the host
