@@ -294,8 +294,15 @@ __device__ __forceinline__ void logit_noise(uint64_t seed, int64_t ge, int64_t p
 // Uniform: k = (u32 * n) >> 32 over ascending legal actions.  Gumbel: argmax
 // of logit + Gumbel over legal actions, ties to the smaller action index.
 // u_pre: the uniform policy's Philox word when the caller drew it already.
+struct Pick {
+    uint64_t seed;
+    int64_t env_base;
+    const float* logits;  // [n,10000] or nullptr (virtual N(0,1) logits)
+    int policy;
+};
+
 template <int POL>
-__device__ void choose(const KArgs& a, const uint16_t* rays, int n, int64_t e, int64_t ply,
+__device__ void choose(const Pick& a, const uint16_t* rays, int n, int64_t e, int64_t ply,
                        int lane, int& act, float& lp, int16_t* acts = nullptr, const uint32_t* u_pre = nullptr) {
     const int64_t ge = a.env_base + e;
     if (n == 0) {
@@ -332,13 +339,17 @@ __device__ void choose(const KArgs& a, const uint16_t* rays, int n, int64_t e, i
             s += expf(z - m);
         }
     };
-    if (acts && n <= 256) {
+    // one visit loop (so the noise code is generated once): over the
+    // shared-memory list, or over the lane's own squares when the list
+    // does not fit
+    const bool listed = acts && n <= 256;
+    if (listed) {
         // spread the legal actions evenly over the lanes: list them in
         // ascending order in shared memory, then lane i takes i, i+32, ...
         int base = 0;
-#pragma unroll
+#pragma unroll 1
         for (int k = 0; k < 4; ++k) {
-            const int c = cnt[k];
+            const int c = k == 0 ? cnt[0] : (k == 1 ? cnt[1] : (k == 2 ? cnt[2] : cnt[3]));
             int incl = c;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -349,22 +360,37 @@ __device__ void choose(const KArgs& a, const uint16_t* rays, int n, int64_t e, i
             if (c) {
                 const uint32_t r = rays[sq];
                 const int pos = base + incl - c;
+#pragma unroll 1
                 for (int j = 0; j < c; ++j) acts[pos + j] = (int16_t)(sq * 100 + decode_ray(sq, r, j));
             }
             base += __shfl_sync(FULL, incl, 31);
         }
         __syncwarp();
-        for (int i = lane; i < n; i += 32) visit(acts[i]);
-        __syncwarp();
-    } else {
-        for (int k = 0; k < 4; ++k) {
-            const int sq = lane + 32 * k;
-            if (sq >= NSQ || cnt[k] == 0) continue;
-            const uint32_t r = rays[sq];
-            for (int j = 0; j < cnt[k]; ++j) visit(sq * 100 + decode_ray(sq, r, j));
-        }
     }
-#pragma unroll
+    int i = lane, k = 0, j = 0;
+#pragma unroll 1
+    for (;;) {
+        int ac;
+        if (listed) {
+            if (i >= n) break;
+            ac = acts[i];
+            i += 32;
+        } else {
+            for (;;) {  // (a select chain keeps cnt[] in registers)
+                const int ck = k == 0 ? cnt[0] : (k == 1 ? cnt[1] : (k == 2 ? cnt[2] : (k == 3 ? cnt[3] : 0x7fffffff)));
+                if (j < ck) break;
+                ++k;
+                j = 0;
+            }
+            if (k == 4) break;
+            const int sq = lane + 32 * (k & 3);
+            ac = sq * 100 + decode_ray(sq, rays[sq], j);
+            ++j;
+        }
+        visit(ac);
+    }
+    __syncwarp();
+#pragma unroll 1
     for (int o = 16; o; o >>= 1) {
         const float ob = __shfl_xor_sync(FULL, best, o), oz = __shfl_xor_sync(FULL, bestz, o);
         const int oa = __shfl_xor_sync(FULL, besta, o);
@@ -382,6 +408,18 @@ __device__ void choose(const KArgs& a, const uint16_t* rays, int n, int64_t e, i
     }
     act = besta;
     lp = bestz - (m + logf(s));
+}
+
+// choose() for the start of a ply whose proposal was not cached (after a
+// host-side change of the state, or logits in memory): one out-of-line copy,
+// so the hot per-ply proposal keeps the kernel's instruction footprint.
+// The policy's inputs come as scalars (not the kernel's argument block,
+// whose address would need a local-memory copy).
+template <int POL>
+__device__ __noinline__ void choose_cold(uint64_t seed, int64_t env_base, const float* logits, int policy,
+                                         const uint16_t* rays, int n, int64_t e, int64_t ply, int lane, int& act,
+                                         float& lp, int16_t* acts) {
+    choose<POL>(Pick{seed, env_base, logits, policy}, rays, n, e, ply, lane, act, lp, acts);
 }
 
 // ---------------------------------------------------------------------------
@@ -955,20 +993,47 @@ __device__ void mask_scatter(const uint16_t* rays, int lane, uint8_t* m) {
 // Legal mask (csrc/stratego_buffer.cu:448-507) of the side to move, built
 // bit-packed in shared memory from the rays (bit j of byte k = flat action
 // 8k+j), then written as bit-packed rows and / or expanded to u8 rows in
-// whole 16-byte chunks.
+// whole 16-byte chunks.  Lane i takes the i-th square with moves (ascending;
+// a second round above 32) and ORs in its piece's whole destination set at
+// once: the row run [sq-left, sq+right] and the column comb sq-10*up ..
+// sq+10*down (stride 10), less sq itself, as one 128-bit value placed at bit
+// sq*100 (its first word is word sq*100/32; adjacent squares can share a
+// word, hence the atomics).
 __device__ void build_mask_bits(const uint16_t* rays, int lane, uint32_t* w) {
+    using u128 = unsigned __int128;
+    // bits 0, 10, 20, ..., 120
+    constexpr uint64_t COMB_LO = 0x1004010040100401ull, COMB_HI = 0x0100401004010040ull;
     for (int i = lane; i < 79; i += 32) reinterpret_cast<uint4*>(w)[i] = make_uint4(0, 0, 0, 0);
-    __syncwarp();
+    uint32_t has[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int sq = lane + 32 * k;
-        if (sq >= NSQ) continue;
-        const uint32_t r = rays[sq];
-        if (!r) continue;
-        const int n = (r & 15) + ((r >> 4) & 15) + ((r >> 8) & 15) + (r >> 12);
-        for (int j = 0; j < n; ++j) {
-            const int f = sq * 100 + decode_ray(sq, r, j);
-            atomicOr(&w[f >> 5], 1u << (f & 31));
+        has[k] = __ballot_sync(FULL, sq < NSQ && rays[sq] != 0);
+    }
+    __syncwarp();
+    const int c0 = __popc(has[0]), c01 = c0 + __popc(has[1]), c012 = c01 + __popc(has[2]);
+    const int np = c012 + __popc(has[3]);
+#pragma unroll 1
+    for (int base = 0; base < np; base += 32) {
+        const int i = base + lane;
+        if (i < np) {
+            const int wi = i < c0 ? 0 : (i < c01 ? 1 : (i < c012 ? 2 : 3));
+            const int k = i - (wi == 0 ? 0 : (wi == 1 ? c0 : (wi == 2 ? c01 : c012)));
+            const uint32_t m = wi == 0 ? has[0] : (wi == 1 ? has[1] : (wi == 2 ? has[2] : has[3]));
+            const int sq = 32 * wi + nth_bit(m, k);
+            const uint32_t r = rays[sq];
+            const int up = r & 15, left = (r >> 4) & 15, right = (r >> 8) & 15, down = r >> 12;
+            const int f0 = sq * 100, b = f0 & 31;
+            const int p = b + sq;  // bit of the piece's own square (never set)
+            const u128 one = 1;
+            const u128 run = (u128)((1u << (left + right + 1)) - 1u) << (p - left);
+            const u128 comb = ((((u128)COMB_HI) << 64) | COMB_LO) & ((one << (10 * (up + down) + 1)) - 1);
+            const u128 x = (run | (comb << (p - 10 * up))) & ~(one << p);
+            uint32_t* wq = w + (f0 >> 5);
+            atomicOr(wq, (uint32_t)x);
+            atomicOr(wq + 1, (uint32_t)(x >> 32));
+            atomicOr(wq + 2, (uint32_t)(x >> 64));
+            atomicOr(wq + 3, (uint32_t)(x >> 96));
         }
     }
     __syncwarp();
@@ -985,10 +1050,27 @@ __device__ void write_mask_u8(const uint32_t* w, int lane, uint8_t* g) {
     }
 }
 
+// One bit-packed row (1250 bytes, 2-byte aligned: rows of consecutive envs
+// are 1250 bytes apart): the 16-byte-aligned middle as 16-byte stores, read
+// from shared memory at the row's 2-byte phase with funnel shifts; the
+// partial chunks at either end as 2-byte stores.
 __device__ void write_mask_bits(const uint32_t* w, int lane, uint8_t* g) {
-    const uint16_t* src = reinterpret_cast<const uint16_t*>(w);
-    uint16_t* dst = reinterpret_cast<uint16_t*>(g);
-    for (int i = lane; i < SB_MASK_BITS_BYTES / 2; i += 32) dst[i] = src[i];
+    const int a = (int)(reinterpret_cast<uintptr_t>(g) & 15);  // even
+    const int head = (16 - a) & 15;                             // bytes before the first aligned chunk
+    const int nfull = (SB_MASK_BITS_BYTES - head) >> 4;
+    const int tail = head + 16 * nfull;
+    const uint16_t* s16 = reinterpret_cast<const uint16_t*>(w);
+    uint16_t* g16 = reinterpret_cast<uint16_t*>(g);
+    if (lane < head / 2) g16[lane] = s16[lane];
+    if (lane < (SB_MASK_BITS_BYTES - tail) / 2) g16[tail / 2 + lane] = s16[tail / 2 + lane];
+    const int sh = (head & 3) * 8;  // 0 or 16
+    for (int c = lane; c < nfull; c += 32) {
+        const int o = head + 16 * c;
+        const uint32_t* q = w + (o >> 2);  // q[4] lies inside the 1264-byte bit buffer
+        const uint32_t v0 = q[0], v1 = q[1], v2 = q[2], v3 = q[3], v4 = q[4];
+        st16(g + o, make_uint4(__funnelshift_r(v0, v1, sh), __funnelshift_r(v1, v2, sh), __funnelshift_r(v2, v3, sh),
+                               __funnelshift_r(v3, v4, sh)));
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -1208,7 +1290,8 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                             n_legal = enumerate(rec, pm, rays, lane);
                             if (!a.actions) {
                                 int ac;
-                                choose<kPol>(a, rays, n_legal, e, ply, lane, ac, lp, acts);
+                                choose_cold<kPol>(a.seed, a.env_base, a.logits, a.policy, rays, n_legal, e, ply, lane, ac,
+                                                  lp, acts);
                                 act = ac;
                             }
                         }
@@ -1275,7 +1358,8 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
             if (has(F_PROPOSE) || has(F_SAMPLE_OUT)) {
                 int ac;
                 float lp;
-                choose<kPol>(a, rays, n, e, pp, lane, ac, lp, acts, kPol == SB_POLICY_UNIFORM ? &u_prop : nullptr);
+                choose<kPol>(Pick{a.seed, a.env_base, a.logits, a.policy}, rays, n, e, pp, lane, ac, lp, acts,
+                             kPol == SB_POLICY_UNIFORM ? &u_prop : nullptr);
                 if (lane == 0) {
                     if (has(F_PROPOSE)) {
                         fld<int16_t>(rec, R_PROP) = (int16_t)ac;

@@ -256,6 +256,8 @@ def timed_launches(ctx: Ctx, launch, k: int, flush_mib: int):
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(k)]
     ctx.barrier()
     torch.cuda.synchronize(ctx.dev)
+    # the NVTX range lets a profiler select the timed launches (ncu --nvtx --nvtx-include timed/)
+    torch.cuda.nvtx.range_push("timed")
     with ClockSampler(ctx.dev) as clocks:
         for i in range(k):
             if flush is not None:
@@ -268,6 +270,7 @@ def timed_launches(ctx: Ctx, launch, k: int, flush_mib: int):
             ends[i].record(ctx.stream)
         torch.cuda.synchronize(ctx.dev)
         ctx.barrier()
+    torch.cuda.nvtx.range_pop()
     total_ms = ctx.max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(starts, ends)))
     return total_ms, clocks.summary()
 
@@ -373,7 +376,9 @@ def run_traj_config(ctx: Ctx) -> dict:
 
     a = ctx.args
     B = a.envs if a.envs != 4096 else 32768
-    T, R = 128, a.plies_per_launch
+    T, R = a.ring_slots, a.plies_per_launch
+    if T <= R:
+        raise SystemExit("--ring-slots must exceed --plies-per-launch")
     buf = StrategoRolloutBuffer(B, ctx.local, seed=SEED, env_base=ctx.rank * B, pool_size=POOL, pool_seed=SEED)
     buf.reset_all_from_pool()
     tr = TrajectoryBuffer(buf, T, policy="gumbel")
@@ -424,7 +429,7 @@ def run_search_config(ctx: Ctx) -> dict:
     from ataraxos_b200.trajectory import BeliefRollouts
 
     a = ctx.args
-    n_roots, k, depth = 64, 1000, 40
+    n_roots, k, depth = 64, a.samples, 40
     roots = StrategoRolloutBuffer(n_roots, ctx.local, seed=SEED, env_base=ctx.rank * n_roots, pool_size=POOL,
                                   pool_seed=SEED)
     roots.reset_all_from_pool()
@@ -479,6 +484,8 @@ def main() -> None:
     ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=2)
     ap.add_argument("--envs", type=int, default=4096, help="envs per GPU (config 2)")
     ap.add_argument("--plies-per-launch", type=int, default=8, help="config 4 rollout launch length")
+    ap.add_argument("--ring-slots", type=int, default=128, help="config 4 ring length T (smaller: profiling cases)")
+    ap.add_argument("--samples", type=int, default=1000, help="config 5 belief samples per root")
     ap.add_argument("--e2e-steps", type=int, default=500)
     ap.add_argument("--e2e-api", choices=["serve", "step_host"], default="step_host",
                     help="host API of the e2e loop: the persistent step server or step_host")
