@@ -291,6 +291,14 @@ def e2e_loop(ctx: Ctx, buf, steps: int, policy: str = "uniform", total_envs: int
     B = buf.n_games
     total = ctx.world * B if total_envs is None else total_envs
     r = buf.step_host(None, policy=policy)
+    # untimed warm-up of the same host loop for about half a second (the
+    # host round trips of a process that has just started run slower)
+    h_act = torch.empty(B, dtype=torch.int64, pin_memory=True)
+    t_end, i = time.perf_counter() + 0.5, 0
+    while i < ctx.args.warmup or time.perf_counter() < t_end:
+        h_act.copy_(r.next_action)
+        r = buf.step_host(h_act, policy=policy)
+        i += 1
     ctx.barrier()
     torch.cuda.synchronize(ctx.dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -306,7 +314,6 @@ def e2e_loop(ctx: Ctx, buf, steps: int, policy: str = "uniform", total_envs: int
         e1.record(st)
         api = "StrategoRolloutBuffer.serve().step (persistent step server)"
     else:
-        h_act = torch.empty(B, dtype=torch.int64, pin_memory=True)
         e0.record(ctx.stream)
         for _ in range(steps):
             h_act.copy_(r.next_action)
