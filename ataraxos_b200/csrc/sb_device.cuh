@@ -114,8 +114,80 @@ __device__ __forceinline__ uint32_t mulshift(uint32_t u, uint32_t n) {
     return (uint32_t)(((uint64_t)u * (uint64_t)n) >> 32);
 }
 
-__device__ __forceinline__ float u01(uint32_t w) {
-    return ((float)(w >> 8) + 0.5f) * (1.0f / 16777216.0f);
+// ---- Float functions of the sampling noise ---------------------------------
+// Written so that the CPU oracle reproduces them bit for bit: every step is
+// one IEEE round-to-nearest operation, spelled as an explicit intrinsic so
+// the compiler fuses or reorders nothing, and the oracle performs the same
+// steps in the same order.  Methods: the natural log by reduction to
+// m in [sqrt(1/2), sqrt(2)) and the series ln m = 2 atanh(s), s = (m-1)/(m+1),
+// to s^11; cos(2 pi u) by quadrant and reflection to theta = (pi/2) h,
+// h in [0, 1/2], and the Taylor series of cos (to theta^10) and sin (to
+// theta^9); exp by z = k ln2 + r (k = rint(z log2 e), ln2 split in two) and
+// the Taylor series of e^r to r^7, scaled by 2^k in the exponent field.
+// Truncation errors are below 2e-9 (relative); rounding adds a few ulp.
+
+// Uniform in the open interval: (w >> 9) + 1/2 over 2^23, a multiple of 2^-24
+// in [2^-24, 1 - 2^-24] (exact in float, never 0 or 1).
+__device__ __forceinline__ float unit_open(uint32_t w) {
+    return __fmul_rn(__fadd_rn((float)(w >> 9), 0.5f), 0x1.0p-23f);
+}
+
+// ln x for a positive normal float x.
+__device__ __forceinline__ float xln(float x) {
+    const uint32_t bx = __float_as_uint(x);
+    const int e = (int)(bx - 0x3F3504F3u) >> 23;  // x / 2^e in [sqrt(1/2), sqrt(2))
+    const float m = __uint_as_float(bx - ((uint32_t)e << 23));
+    const float t = __fsub_rn(m, 1.0f);           // exact
+    const float s = __fdiv_rn(t, __fadd_rn(t, 2.0f));
+    const float y = __fmul_rn(s, s);
+    float p = 0x1.745d18p-3f;                     // 2/11
+    p = __fmaf_rn(p, y, 0x1.c71c72p-3f);          // 2/9
+    p = __fmaf_rn(p, y, 0x1.24924ap-2f);          // 2/7
+    p = __fmaf_rn(p, y, 0x1.99999ap-2f);          // 2/5
+    p = __fmaf_rn(p, y, 0x1.555556p-1f);          // 2/3
+    p = __fmaf_rn(p, y, 2.0f);
+    return __fmaf_rn((float)e, 0x1.62e43p-1f, __fmul_rn(s, p));
+}
+
+// cos(2 pi u) for u in (0, 1) a multiple of 2^-24.
+__device__ __forceinline__ float xcos2pi(float u) {
+    const float v = __fmul_rn(u, 4.0f);  // exact
+    const int q = (int)v;                // quadrant 0..3
+    const float r = __fsub_rn(v, (float)q);
+    const bool low = r <= 0.5f;
+    const float h = low ? r : __fsub_rn(1.0f, r);
+    const float y = __fmul_rn(h, h);
+    float c = -0x1.a6d1f2p-16f;          // cos(pi h / 2) = sum (-1)^k (pi/2)^2k h^2k / (2k)!
+    c = __fmaf_rn(c, y, 0x1.e1f506p-11f);
+    c = __fmaf_rn(c, y, -0x1.55d3c8p-6f);
+    c = __fmaf_rn(c, y, 0x1.03c1f0p-2f);
+    c = __fmaf_rn(c, y, -0x1.3bd3ccp+0f);
+    c = __fmaf_rn(c, y, 1.0f);
+    float sn = 0x1.507834p-13f;          // sin(pi h / 2) = h sum (-1)^k (pi/2)^(2k+1) h^2k / (2k+1)!
+    sn = __fmaf_rn(sn, y, -0x1.32d2ccp-8f);
+    sn = __fmaf_rn(sn, y, 0x1.466bc6p-4f);
+    sn = __fmaf_rn(sn, y, -0x1.4abbcep-1f);
+    sn = __fmaf_rn(sn, y, 0x1.921fb6p+0f);
+    sn = __fmul_rn(sn, h);
+    const float cr = low ? c : sn, sr = low ? sn : c;  // cos / sin of (pi/2) r
+    return q == 0 ? cr : (q == 1 ? -sr : (q == 2 ? -cr : sr));
+}
+
+// e^z for z <= 88 (0 below -80).
+__device__ __forceinline__ float xexp(float z) {
+    if (z < -80.0f) return 0.0f;
+    const float k = rintf(__fmul_rn(z, 0x1.715476p+0f));
+    float r = __fmaf_rn(-k, 0x1.62e43p-1f, z);
+    r = __fmaf_rn(-k, -0x1.05c61p-29f, r);
+    float p = 0x1.a01a02p-13f;  // 1/7!
+    p = __fmaf_rn(p, r, 0x1.6c16c2p-10f);
+    p = __fmaf_rn(p, r, 0x1.111112p-7f);
+    p = __fmaf_rn(p, r, 0x1.555556p-5f);
+    p = __fmaf_rn(p, r, 0x1.555556p-3f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    return __uint_as_float(__float_as_uint(p) + ((uint32_t)(int)k << 23));
 }
 
 __device__ __forceinline__ uint64_t warp_xor64(uint64_t v) {

@@ -282,17 +282,21 @@ __device__ int kth_action(int kth, const uint16_t* rays, int lane) {
 }
 
 
-// Virtual N(0,1) logit (Box-Muller) and Gumbel noise of action `act`.
-__device__ __forceinline__ void logit_noise(uint64_t seed, int64_t ge, int64_t ply, int act, float& z, float& g) {
-    const uint4 w = philox((uint32_t)ge, (uint32_t)ply, (uint32_t)act, TAG_LOGIT, seed);
-    const float u1 = u01(w.x), u2 = u01(w.y), u3 = u01(w.z);
-    z = sqrtf(-2.0f * logf(u1)) * cosf(6.2831853071795864f * u2);
-    g = -logf(-logf(u3));
-}
-
 // Choose an action for the current state (rays already enumerated, n moves).
-// Uniform: k = (u32 * n) >> 32 over ascending legal actions.  Gumbel: argmax
-// of logit + Gumbel over legal actions, ties to the smaller action index.
+// Uniform: k = (u32 * n) >> 32 over ascending legal actions, log-prob -ln n.
+// Softmax policy (SB_POLICY_GUMBEL): action a has logit z_a (from memory, or
+// virtual N(0,1): Box-Muller on Philox(seed; env, ply, a, TAG_LOGIT) words
+// x, y) and an Exp(1) variate E_a = -ln(word z); the choice is the legal a
+// with the largest q_a / E_a, q_a = e^(z_a - c) (c = 0 for virtual logits,
+// the legal maximum for logits in memory), ties to the smaller action index.
+// That is Gumbel-max: ln(q_a / E_a) = z_a - c + G_a with G_a = -ln E_a
+// Gumbel(0,1), so a is drawn from the softmax of the legal logits.  The
+// log-prob is z_a - c - ln(sum of q over legal actions).  The sum's order is
+// fixed: lane L adds its actions in ascending order (lane L takes list
+// entries L, L+32, ... of the ascending legal list, or, above 256 legal
+// moves, the moves of squares L, L+32, L+64, L+96), then a butterfly over
+// the lanes (xor 16, 8, 4, 2, 1); with the float functions above, every
+// value is reproduced bit for bit by the CPU oracle.
 // u_pre: the uniform policy's Philox word when the caller drew it already.
 struct Pick {
     uint64_t seed;
@@ -315,30 +319,11 @@ __device__ void choose(const Pick& a, const uint16_t* rays, int n, int64_t e, in
         const uint32_t u =
             u_pre ? *u_pre : philox((uint32_t)ge, (uint32_t)ply, (uint32_t)((uint64_t)ply >> 32), TAG_ACTION, a.seed).x;
         act = kth_action((int)mulshift(u, (uint32_t)n), rays, lane);
-        lp = -logf((float)n);
+        lp = -xln((float)n);
         return;
     }
     int cnt[4];
     ray_counts(rays, lane, cnt);
-    float best = -INFINITY, bestz = 0.0f, m = -INFINITY, s = 0.0f;
-    int besta = 0x7fffffff;
-    auto visit = [&](int ac) {
-        float z, g;
-        logit_noise(a.seed, ge, ply, ac, z, g);
-        if (a.logits) z = a.logits[e * NACT + ac];
-        const float key = z + g;
-        if (key > best || (key == best && ac < besta)) {
-            best = key;
-            besta = ac;
-            bestz = z;
-        }
-        if (z > m) {
-            s = s * expf(m - z) + 1.0f;
-            m = z;
-        } else {
-            s += expf(z - m);
-        }
-    };
     // one visit loop (so the noise code is generated once): over the
     // shared-memory list, or over the lane's own squares when the list
     // does not fit
@@ -367,27 +352,55 @@ __device__ void choose(const Pick& a, const uint16_t* rays, int n, int64_t e, in
         }
         __syncwarp();
     }
-    int i = lane, k = 0, j = 0;
+    const float* lg = a.logits ? a.logits + e * NACT : nullptr;
+    float shift = 0.0f;  // c: 0, or the legal maximum of the logits in memory
+    float best = -1.0f, bestz = 0.0f, s = 0.0f;
+    int besta = 0x7fffffff;
+    // pass 0 (logits in memory only): their legal maximum; pass 1: the choice
 #pragma unroll 1
-    for (;;) {
-        int ac;
-        if (listed) {
-            if (i >= n) break;
-            ac = acts[i];
-            i += 32;
-        } else {
-            for (;;) {  // (a select chain keeps cnt[] in registers)
-                const int ck = k == 0 ? cnt[0] : (k == 1 ? cnt[1] : (k == 2 ? cnt[2] : (k == 3 ? cnt[3] : 0x7fffffff)));
-                if (j < ck) break;
-                ++k;
-                j = 0;
+    for (int pass = lg ? 0 : 1; pass < 2; ++pass) {
+        float mx = -INFINITY;
+        int i = lane, k = 0, j = 0;
+#pragma unroll 1
+        for (;;) {
+            int ac;
+            if (listed) {
+                if (i >= n) break;
+                ac = acts[i];
+                i += 32;
+            } else {
+                for (;;) {  // (a select chain keeps cnt[] in registers)
+                    const int ck = k == 0 ? cnt[0] : (k == 1 ? cnt[1] : (k == 2 ? cnt[2] : (k == 3 ? cnt[3] : 0x7fffffff)));
+                    if (j < ck) break;
+                    ++k;
+                    j = 0;
+                }
+                if (k == 4) break;
+                const int sq = lane + 32 * (k & 3);
+                ac = sq * 100 + decode_ray(sq, rays[sq], j);
+                ++j;
             }
-            if (k == 4) break;
-            const int sq = lane + 32 * (k & 3);
-            ac = sq * 100 + decode_ray(sq, rays[sq], j);
-            ++j;
+            if (pass == 0) {
+                mx = fmaxf(mx, lg[ac]);
+                continue;
+            }
+            const uint4 w = philox((uint32_t)ge, (uint32_t)ply, (uint32_t)ac, TAG_LOGIT, a.seed);
+            const float z = lg ? lg[ac]
+                               : __fmul_rn(__fsqrt_rn(__fmul_rn(-2.0f, xln(unit_open(w.x)))), xcos2pi(unit_open(w.y)));
+            const float q = xexp(__fsub_rn(z, shift));
+            const float key = __fdiv_rn(q, -xln(unit_open(w.z)));
+            if (key > best || (key == best && ac < besta)) {
+                best = key;
+                besta = ac;
+                bestz = z;
+            }
+            s = __fadd_rn(s, q);
         }
-        visit(ac);
+        if (pass == 0) {
+#pragma unroll
+            for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+            shift = mx;
+        }
     }
     __syncwarp();
 #pragma unroll 1
@@ -399,15 +412,10 @@ __device__ void choose(const Pick& a, const uint16_t* rays, int n, int64_t e, in
             besta = oa;
             bestz = oz;
         }
-        const float om = __shfl_xor_sync(FULL, m, o), os = __shfl_xor_sync(FULL, s, o);
-        const float M = fmaxf(m, om);
-        if (M != -INFINITY) {
-            s = (m == -INFINITY ? 0.0f : s * expf(m - M)) + (om == -INFINITY ? 0.0f : os * expf(om - M));
-            m = M;
-        }
+        s = __fadd_rn(s, __shfl_xor_sync(FULL, s, o));
     }
     act = besta;
-    lp = bestz - (m + logf(s));
+    lp = __fsub_rn(__fsub_rn(bestz, shift), xln(s));
 }
 
 // choose() for the start of a ply whose proposal was not cached (after a

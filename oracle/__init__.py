@@ -44,7 +44,7 @@ def build(force: bool = False) -> Path:
     if force or not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < SRC.stat().st_mtime:
         tmp = LIB_PATH.with_suffix(f".{os.getpid()}.tmp")
         subprocess.run(
-            ["gcc", "-O2", "-std=c11", "-Wall", "-shared", "-fPIC", "-o", str(tmp), str(SRC), "-lpthread", "-lm"],
+            ["gcc", "-O2", "-std=c11", "-ffp-contract=off", "-Wall", "-shared", "-fPIC", "-o", str(tmp), str(SRC), "-lpthread", "-lm"],
             check=True,
         )
         os.replace(tmp, LIB_PATH)
@@ -116,6 +116,7 @@ def lib() -> ctypes.CDLL:
             "or_belief_resample": (None, [S, S, vp, C]),
             "or_f32_to_bf16": (ctypes.c_uint16, [ctypes.c_float]),
             "or_logit_noise": (None, [u64, i64, i64, ctypes.c_int32, vp, vp]),
+            "or_noise_fn": (ctypes.c_float, [ctypes.c_int, ctypes.c_float]),
         }
         for name, (res, args) in sig.items():
             f = getattr(_lib, name)
@@ -340,6 +341,11 @@ def fraction(num: int, den: int) -> float:
 
 def f32_to_bf16_bits(x: float) -> int:
     return int(lib().or_f32_to_bf16(x))
+
+
+def noise_fn(which: str, x: float) -> float:
+    """The sampler's float functions: "ln", "cos2pi", "exp" (bit-identical to the kernel's)."""
+    return float(lib().or_noise_fn({"ln": 0, "cos2pi": 1, "exp": 2}[which], x))
 
 
 def logit_noise(seed: int, genv: int, ply: int, action: int) -> tuple[float, float]:

@@ -4,8 +4,9 @@
   the ring must equal what the oracle produces ply by ply (uniform policy:
   bit-exact observations, masks, actions, rewards, dones; log-probs to 1e-6),
   including wrap-around of the ring;
-* Gumbel-policy rollouts replay legally on the oracle and their log-probs
-  match log-softmax of the virtual logits;
+* Gumbel-policy rollouts: the oracle's proposals with bit-identical
+  log-probs ply by ply (which also match log-softmax of the virtual logits),
+  replayed legally on the oracle;
 * ``resample_from`` (belief resampling) is bit-exact with the oracle's
   restatement and keeps everything the side to move knows.
 """
@@ -92,6 +93,10 @@ def test_trajectory_gumbel_replays_on_oracle():
     lps = tr.logprob.cpu().numpy()
     dones = tr.done.cpu().numpy()
     for p in range(plies):
+        # the rollout's proposals are the oracle's, bit for bit
+        oa, olp, _ = o.sample(ply=p, policy=oracle.POLICY_GUMBEL)
+        np.testing.assert_array_equal(acts[p], oa, err_msg=f"ply {p}")
+        np.testing.assert_array_equal(lps[p].view(np.uint32), olp.view(np.uint32), err_msg=f"ply {p}")
         if p % 10 == 0:  # log-prob of the chosen action = log-softmax of the virtual logits
             for g in range(0, n, 17):
                 legal = o.legal_list(g)
