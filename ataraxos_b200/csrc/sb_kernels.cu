@@ -225,7 +225,7 @@ __device__ __noinline__ int enumerate(const uint8_t* b, int p, uint16_t* rays, i
             total += up + left + right + down;
         }
     }
-    total = warp_sum(total);
+    total = __reduce_add_sync(FULL, total);
     __syncwarp();
     return total;
 }
@@ -932,8 +932,10 @@ __device__ void write_info_dense(const uint8_t* rec, const KArgs& a, int lane, u
 }
 
 // Sparse planes: 0-11 (one 1 per own piece) and 456-487 (the k-th most recent
-// move's +1 at dst, -1 at src).  Their zero rows are written here unless a
-// producer warp already streamed them (kZerosDone); the non-zeros follow.
+// move's +1 at dst, -1 at src).  Without a producer warp, planes 0-11 are
+// written as whole rows and the history planes as zero rows; after a
+// producer warp streamed all their zero rows (kZerosDone), only the non-zeros
+// are stored.  The history non-zeros follow in both cases.
 // DENSE_ALL also zeroes planes 43-455.
 template <typename T, bool kZerosDone>
 __device__ void write_info_sparse(const uint8_t* rec, int lane, uint8_t* g, int hist_off, bool all) {
@@ -941,20 +943,25 @@ __device__ void write_info_sparse(const uint8_t* rec, int lane, uint8_t* g, int 
     constexpr int PB = InfoGeom<T>::PB;
     if (lane < 25) {
         uint8_t* gl = g + lane * 4 * (int)sizeof(T);
+        const SqFeat f = square_features(rec, lane);
         if (!kZerosDone) {
-            const typename Q::V Z = Q::splat(0u);
+            // own pieces (planes 0-11) as whole rows, one byte compare per
+            // type; the move-history planes as zero rows
+            const uint32_t ONE = Q::bits(IV<T>::from(1.0f));
 #pragma unroll
-            for (int t = 0; t < 12; ++t) Q::st(gl + t * PB, Z);
+            for (int t = 0; t < 12; ++t)
+                Q::st(gl + t * PB, Q::ones(__vcmpeq4(f.ot, (uint32_t)(t + 1) * 0x01010101u) & 0x01010101u, ONE));
+            const typename Q::V Z = Q::splat(0u);
 #pragma unroll 8
             for (int k = 0; k < 32; ++k) Q::st(gl + hist_off + k * PB, Z);
-        }
-        // own one-hots: same lane as its zero row, so program order suffices
-        const SqFeat f = square_features(rec, lane);
-        T* g1 = reinterpret_cast<T*>(g);
+        } else {
+            // own one-hots on the producer's zero rows
+            T* g1 = reinterpret_cast<T*>(g);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const uint32_t pc = (f.ot >> (8 * j)) & 0xFF;
-            if (pc) g1[(pc - 1) * NSQ + 4 * lane + j] = IV<T>::from(1.0f);
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t pc = (f.ot >> (8 * j)) & 0xFF;
+                if (pc) g1[(pc - 1) * NSQ + 4 * lane + j] = IV<T>::from(1.0f);
+            }
         }
     }
     __syncwarp();
