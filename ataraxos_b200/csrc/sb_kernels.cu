@@ -1266,6 +1266,10 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
         }
 
         for (int p = 0; p < np; ++p, ++iter) {
+            // outside MODE_STEP_PROD the CTA's warps start each ply together:
+            // they then run the same code and write neighbouring envs' rows
+            // at about the same time (measured faster than letting them drift)
+            if (!kProd) __syncthreads();
             const int64_t ply = ply_base + p;
             const int64_t s_cur = (a.slot0 + p) % a.n_slots;
             const int64_t s_next = has(F_APPLY) ? (a.slot0 + p + 1) % a.n_slots : a.slot0 % a.n_slots;
