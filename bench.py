@@ -205,13 +205,17 @@ def run_reference(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
-def _profile_traffic(name: str) -> float | None:
-    """dram_bytes_per_launch recorded from the ncu capture summarised in profiles/<name>."""
+def _profile_traffic(name: str, updates_per_launch: int | None = None) -> float | None:
+    """DRAM bytes (read + write) per launch from the ncu capture summarised in
+    profiles/<name>: its dram_bytes_per_launch, or, for a capture taken on a
+    smaller case, its dram_bytes_per_update times the updates of this launch."""
     f = ROOT / "profiles" / name
     try:
         for line in f.read_text().splitlines():
-            if line.startswith("dram_bytes_per_launch:"):
+            if line.startswith("dram_bytes_per_launch:") and updates_per_launch is None:
                 return float(line.split(":", 1)[1].split()[0])
+            if line.startswith("dram_bytes_per_update:") and updates_per_launch is not None:
+                return float(line.split(":", 1)[1].split()[0]) * updates_per_launch
     except Exception:
         return None
     return None
@@ -370,7 +374,8 @@ def run_step_config(ctx: Ctx, cfg: int) -> dict:
                                 "d2h_bytes_per_step": d2h, "api": api},
         "gpu_launches": a.steps, "config": {"workload": workload, "envs_per_gpu": B, "l2": l2,
                                             "parallelism": f"env-sharded x{ctx.world}, no step-path collective"},
-        "scaling": scaling, "traffic": _profile_traffic("step_kernel_config2.txt") if cfg == 2 else None,
+        "scaling": scaling,
+        "traffic": _profile_traffic("step_kernel_config2.txt") if cfg == 2 else _profile_traffic("step_kernel_config3.txt", B),
     }
 
 
@@ -424,7 +429,7 @@ def run_traj_config(ctx: Ctx) -> dict:
                                f"{R} plies per launch", "envs_per_gpu": B,
                    "l2": f"ring of {T} slots ({T * B * 16.5 / 1e9:.0f} GB) far above L2; no flush",
                    "parallelism": f"env-sharded x{ctx.world}, no step-path collective"},
-        "scaling": "weak", "traffic": None,
+        "scaling": "weak", "traffic": _profile_traffic("rollout_kernel_config4.txt", B * R),
     }
 
 
@@ -478,7 +483,7 @@ def run_search_config(ctx: Ctx) -> dict:
                                f"{depth}-ply uniform rollouts in one launch; per-ply bit-packed masks, terminal values; "
                                "one step = resample + prime + rollout", "envs_per_gpu": n,
                    "l2": "n/a: per-launch outputs 3.2 GB/GPU", "parallelism": f"root-sharded x{ctx.world}"},
-        "scaling": "weak", "traffic": None,
+        "scaling": "weak", "traffic": _profile_traffic("search_kernels_config5.txt", n * depth),
     }
 
 
