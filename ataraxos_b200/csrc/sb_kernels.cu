@@ -292,11 +292,11 @@ __device__ int kth_action(int kth, const uint16_t* rays, int lane) {
 // That is Gumbel-max: ln(q_a / E_a) = z_a - c + G_a with G_a = -ln E_a
 // Gumbel(0,1), so a is drawn from the softmax of the legal logits.  The
 // log-prob is z_a - c - ln(sum of q over legal actions).  The sum's order is
-// fixed: lane L adds its actions in ascending order (lane L takes list
-// entries L, L+32, ... of the ascending legal list, or, above 256 legal
-// moves, the moves of squares L, L+32, L+64, L+96), then a butterfly over
-// the lanes (xor 16, 8, 4, 2, 1); with the float functions above, every
-// value is reproduced bit for bit by the CPU oracle.
+// fixed: lane L adds the L-th, (L+32)-th, ... legal action (ascending
+// order) in that order, then a butterfly over the lanes (xor 16, 8, 4, 2,
+// 1); with the float functions above, every value is reproduced bit for bit
+// by the CPU oracle.
+// acts: the warp's shared-memory scratch (at least 200 bytes).
 // u_pre: the uniform policy's Philox word when the caller drew it already.
 struct Pick {
     uint64_t seed;
@@ -324,17 +324,16 @@ __device__ void choose(const Pick& a, const uint16_t* rays, int n, int64_t e, in
     }
     int cnt[4];
     ray_counts(rays, lane, cnt);
-    // one visit loop (so the noise code is generated once): over the
-    // shared-memory list, or over the lane's own squares when the list
-    // does not fit
-    const bool listed = acts && n <= 256;
-    if (listed) {
-        // spread the legal actions evenly over the lanes: list them in
-        // ascending order in shared memory, then lane i takes i, i+32, ...
+    // Lane L takes the L-th, (L+32)-th, ... legal action in ascending order:
+    // the inclusive prefix of the per-square move counts goes to shared
+    // memory, and each lane finds the square of its action by binary search
+    // (the first square whose prefix exceeds the action's rank).
+    uint16_t* incl16 = reinterpret_cast<uint16_t*>(acts);  // [100]
+    {
         int base = 0;
-#pragma unroll 1
+#pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const int c = k == 0 ? cnt[0] : (k == 1 ? cnt[1] : (k == 2 ? cnt[2] : cnt[3]));
+            const int c = cnt[k];
             int incl = c;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -342,12 +341,7 @@ __device__ void choose(const Pick& a, const uint16_t* rays, int n, int64_t e, in
                 if (lane >= o) incl += v;
             }
             const int sq = lane + 32 * k;
-            if (c) {
-                const uint32_t r = rays[sq];
-                const int pos = base + incl - c;
-#pragma unroll 1
-                for (int j = 0; j < c; ++j) acts[pos + j] = (int16_t)(sq * 100 + decode_ray(sq, r, j));
-            }
+            if (sq < NSQ) incl16[sq] = (uint16_t)(base + incl);
             base += __shfl_sync(FULL, incl, 31);
         }
         __syncwarp();
@@ -360,26 +354,17 @@ __device__ void choose(const Pick& a, const uint16_t* rays, int n, int64_t e, in
 #pragma unroll 1
     for (int pass = lg ? 0 : 1; pass < 2; ++pass) {
         float mx = -INFINITY;
-        int i = lane, k = 0, j = 0;
 #pragma unroll 1
-        for (;;) {
-            int ac;
-            if (listed) {
-                if (i >= n) break;
-                ac = acts[i];
-                i += 32;
-            } else {
-                for (;;) {  // (a select chain keeps cnt[] in registers)
-                    const int ck = k == 0 ? cnt[0] : (k == 1 ? cnt[1] : (k == 2 ? cnt[2] : (k == 3 ? cnt[3] : 0x7fffffff)));
-                    if (j < ck) break;
-                    ++k;
-                    j = 0;
-                }
-                if (k == 4) break;
-                const int sq = lane + 32 * (k & 3);
-                ac = sq * 100 + decode_ray(sq, rays[sq], j);
-                ++j;
+        for (int t = lane; t < n; t += 32) {
+            int lo = 0, hi = NSQ - 1;
+#pragma unroll
+            for (int it = 0; it < 7; ++it) {  // 2^7 >= 100 squares
+                const int mid = (lo + hi) >> 1;
+                if ((int)incl16[mid] > t) hi = mid;
+                else lo = mid + 1;
             }
+            const uint32_t r = rays[lo];
+            const int ac = lo * 100 + decode_ray(lo, r, t - ((int)incl16[lo] - ray_count(r)));
             if (pass == 0) {
                 mx = fmaxf(mx, lg[ac]);
                 continue;
