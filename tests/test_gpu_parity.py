@@ -206,6 +206,40 @@ def test_gumbel_sampling_matches_oracle():
     assert_state_equal(export_np(b), o.export(), "after gumbel replay")
 
 
+def test_sampling_with_many_legal_moves_matches_oracle():
+    """Custom setups of 28 Scouts give 130-165 legal moves (five or more per
+    lane): uniform and Gumbel choices and log-probs stay bit-identical to the
+    oracle over a few plies."""
+    rng = np.random.default_rng(5)
+    n = 6
+    red = np.zeros((n, 10, 10), np.int8)
+    blue = np.zeros((n, 10, 10), np.int8)
+    lakes = {(4, 2), (4, 3), (5, 2), (5, 3), (4, 6), (4, 7), (5, 6), (5, 7)}
+    for g in range(n):
+        sqs = [(r, c) for r in range(10) for c in range(10) if (r, c) not in lakes]
+        rng.shuffle(sqs)
+        for r, c in sqs[:28]:
+            red[g, r, c] = 2  # Scout
+        blue[g, sqs[28][0], sqs[28][1]] = 11  # Flag
+        for r, c in sqs[29:31]:
+            blue[g, r, c] = 10  # Marshal
+    for policy, opol in (("uniform", oracle.POLICY_UNIFORM), ("gumbel", oracle.POLICY_GUMBEL)):
+        b = _buf(n, seed=41)
+        o = oracle.OracleState(n, seed=41)
+        b.reset_all(torch.from_numpy(red), torch.from_numpy(blue))
+        o.reset_planes(red, blue, force_all=True)
+        assert min(len(o.legal_list(g)) for g in range(n)) > 128
+        for t in range(6):
+            acts, lp = b.sample_actions(policy)
+            oa, olp, _ = o.sample(ply=b.ply, policy=opol)
+            np.testing.assert_array_equal(acts.cpu().numpy(), oa, err_msg=f"{policy} ply {t}")
+            np.testing.assert_array_equal(lp.cpu().numpy().view(np.uint32), olp.view(np.uint32),
+                                          err_msg=f"{policy} ply {t}")
+            b.step(acts.cpu(), auto_reset=False)
+            o.step(oa, auto_reset=False)
+        assert_state_equal(export_np(b), o.export(), f"{policy} many moves")
+
+
 def test_gumbel_with_logits_in_memory_follows_logits():
     n = 64
     pool = oracle.make_setup_pool(4, 256)
