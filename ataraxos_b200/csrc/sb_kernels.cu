@@ -105,7 +105,7 @@ constexpr int SERVE_GO = 0, SERVE_STOP = 1, SERVE_DONE = 16, DEV_DONE_COUNT = 2;
 constexpr int WARPS = 8;  // warps (envs in flight) per CTA
 constexpr int ZOB_N = 2600;  // entries of the [10,10,2,13] Zobrist table
 constexpr int SM_RAYS = 256;   // 100 x uint16 packed rays
-constexpr int SM_ACTS = 576;   // 256 x int16 legal-action list (Gumbel sampling)
+constexpr int SM_SCRATCH = 576;  // 512-byte scratch: the Gumbel sampler's per-square move-count prefix
 constexpr int SM_FIXED = 1088;
 constexpr int SM_BITS = SM_FIXED;  // 1264-byte bit-packed legal mask (mask outputs only)
 constexpr int ZERO_BYTES = 12800;  // MODE_STEP_PROD: per-CTA zero buffer, source of the bulk zero rows
@@ -307,7 +307,7 @@ struct Pick {
 
 template <int POL>
 __device__ void choose(const Pick& a, const uint16_t* rays, int n, int64_t e, int64_t ply,
-                       int lane, int& act, float& lp, int16_t* acts = nullptr, const uint32_t* u_pre = nullptr) {
+                       int lane, int& act, float& lp, uint16_t* scratch = nullptr, const uint32_t* u_pre = nullptr) {
     const int64_t ge = a.env_base + e;
     if (n == 0) {
         act = -1;
@@ -328,7 +328,7 @@ __device__ void choose(const Pick& a, const uint16_t* rays, int n, int64_t e, in
     // the inclusive prefix of the per-square move counts goes to shared
     // memory, and each lane finds the square of its action by binary search
     // (the first square whose prefix exceeds the action's rank).
-    uint16_t* incl16 = reinterpret_cast<uint16_t*>(acts);  // [100]
+    uint16_t* incl16 = scratch;  // [100]
     {
         int base = 0;
 #pragma unroll
@@ -411,8 +411,8 @@ __device__ void choose(const Pick& a, const uint16_t* rays, int n, int64_t e, in
 template <int POL>
 __device__ __noinline__ void choose_cold(uint64_t seed, int64_t env_base, const float* logits, int policy,
                                          const uint16_t* rays, int n, int64_t e, int64_t ply, int lane, int& act,
-                                         float& lp, int16_t* acts) {
-    choose<POL>(Pick{seed, env_base, logits, policy}, rays, n, e, ply, lane, act, lp, acts);
+                                         float& lp, uint16_t* scratch) {
+    choose<POL>(Pick{seed, env_base, logits, policy}, rays, n, e, ply, lane, act, lp, scratch);
 }
 
 // ---------------------------------------------------------------------------
@@ -1182,7 +1182,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
     }
     uint8_t* rec = ws;
     uint16_t* rays = reinterpret_cast<uint16_t*>(ws + SM_RAYS);
-    int16_t* acts = reinterpret_cast<int16_t*>(ws + SM_ACTS);
+    uint16_t* scratch = reinterpret_cast<uint16_t*>(ws + SM_SCRATCH);
     uint32_t* wbits = reinterpret_cast<uint32_t*>(ws + SM_BITS);
     constexpr int PB = InfoGeom<T>::PB;
     const bool compact = a.info_layout == SB_LAYOUT_COMPACT;
@@ -1295,7 +1295,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                             if (!a.actions) {
                                 int ac;
                                 choose_cold<kPol>(a.seed, a.env_base, a.logits, a.policy, rays, n_legal, e, ply, lane, ac,
-                                                  lp, acts);
+                                                  lp, scratch);
                                 act = ac;
                             }
                         }
@@ -1362,7 +1362,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
             if (has(F_PROPOSE) || has(F_SAMPLE_OUT)) {
                 int ac;
                 float lp;
-                choose<kPol>(Pick{a.seed, a.env_base, a.logits, a.policy}, rays, n, e, pp, lane, ac, lp, acts,
+                choose<kPol>(Pick{a.seed, a.env_base, a.logits, a.policy}, rays, n, e, pp, lane, ac, lp, scratch,
                              kPol == SB_POLICY_UNIFORM ? &u_prop : nullptr);
                 if (lane == 0) {
                     if (has(F_PROPOSE)) {
