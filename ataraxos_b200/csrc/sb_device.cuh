@@ -119,8 +119,8 @@ __device__ __forceinline__ uint32_t mulshift(uint32_t u, uint32_t n) {
 // one IEEE round-to-nearest operation, spelled as an explicit intrinsic so
 // the compiler fuses or reorders nothing, and the oracle performs the same
 // steps in the same order.  Methods: the natural log by reduction to
-// m in [sqrt(1/2), sqrt(2)) and the series ln m = 2 atanh(s), s = (m-1)/(m+1),
-// to s^11; cos(2 pi u) by quadrant and reflection to theta = (pi/2) h,
+// m in [sqrt(1/2), sqrt(2)), a 23-entry table of 32nds and the series of
+// ln(1 + r) to r^5; cos(2 pi u) by quadrant and reflection to theta = (pi/2) h,
 // h in [0, 1/2], and the Taylor series of cos (to theta^10) and sin (to
 // theta^9); exp by z = k ln2 + r (k = rint(z log2 e), ln2 split in two) and
 // the Taylor series of e^r to r^7, scaled by 2^k in the exponent field.
@@ -132,21 +132,51 @@ __device__ __forceinline__ float unit_open(uint32_t w) {
     return __fmul_rn(__fadd_rn((float)(w >> 9), 0.5f), 0x1.0p-23f);
 }
 
-// ln x for a positive normal float x.
+// ln x for a positive normal float x: x = 2^e m with m in [sqrt(1/2),
+// sqrt(2)); c = 1 + i/32 is the nearest 32nd to m (i = rint(32 (m - 1)) in
+// -9..13) and the table holds 1/c rounded to float (inv) and -ln(inv)
+// rounded to float (L); then r = m inv - 1 (one rounding, |r| < 0.023) and
+// ln x = e ln2 + L + ln(1 + r), the last by its Taylor series to r^5.  At
+// i = 0 the table entry is exact (inv = 1, L = 0), so values near 1 keep
+// their relative accuracy.
+__device__ const float2 g_lntab[23] = {
+    {0x1.642c86p+0f, -0x1.522ae2p-2f},
+    {0x1.555556p+0f, -0x1.269624p-2f},
+    {0x1.47ae14p+0f, -0x1.f991c4p-3f},
+    {0x1.3b13b2p+0f, -0x1.a93ed8p-3f},
+    {0x1.2f684cp+0f, -0x1.5bf408p-3f},
+    {0x1.24924ap+0f, -0x1.1178eep-3f},
+    {0x1.1a7b96p+0f, -0x1.9335e4p-4f},
+    {0x1.111112p+0f, -0x1.08599ap-4f},
+    {0x1.08421p+0f, -0x1.0415c8p-5f},
+    {0x1p+0f, 0.0f},
+    {0x1.f07c2p-1f, 0x1.f8299p-6f},
+    {0x1.e1e1e2p-1f, 0x1.f0a30ap-5f},
+    {0x1.d41d42p-1f, 0x1.6f0d28p-4f},
+    {0x1.c71c72p-1f, 0x1.e27074p-4f},
+    {0x1.bacf92p-1f, 0x1.29552cp-3f},
+    {0x1.af286cp-1f, 0x1.5ff306p-3f},
+    {0x1.a41a42p-1f, 0x1.9525a8p-3f},
+    {0x1.99999ap-1f, 0x1.c8ff7ap-3f},
+    {0x1.8f9c18p-1f, 0x1.fb918cp-3f},
+    {0x1.861862p-1f, 0x1.1675cap-2f},
+    {0x1.7d05f4p-1f, 0x1.2e8e2cp-2f},
+    {0x1.745d18p-1f, 0x1.4618bap-2f},
+    {0x1.6c16c2p-1f, 0x1.5d1bdap-2f},
+};
 __device__ __forceinline__ float xln(float x) {
     const uint32_t bx = __float_as_uint(x);
     const int e = (int)(bx - 0x3F3504F3u) >> 23;  // x / 2^e in [sqrt(1/2), sqrt(2))
     const float m = __uint_as_float(bx - ((uint32_t)e << 23));
-    const float t = __fsub_rn(m, 1.0f);           // exact
-    const float s = __fdiv_rn(t, __fadd_rn(t, 2.0f));
-    const float y = __fmul_rn(s, s);
-    float p = 0x1.745d18p-3f;                     // 2/11
-    p = __fmaf_rn(p, y, 0x1.c71c72p-3f);          // 2/9
-    p = __fmaf_rn(p, y, 0x1.24924ap-2f);          // 2/7
-    p = __fmaf_rn(p, y, 0x1.99999ap-2f);          // 2/5
-    p = __fmaf_rn(p, y, 0x1.555556p-1f);          // 2/3
-    p = __fmaf_rn(p, y, 2.0f);
-    return __fmaf_rn((float)e, 0x1.62e43p-1f, __fmul_rn(s, p));
+    const int i = __float2int_rn(__fmul_rn(__fsub_rn(m, 1.0f), 32.0f));  // m - 1 and the scaling are exact
+    const float2 t = __ldg(&g_lntab[i + 9]);
+    const float r = __fmaf_rn(m, t.x, -1.0f);
+    float p = 0x1.99999ap-3f;          // 1/5
+    p = __fmaf_rn(p, r, -0.25f);
+    p = __fmaf_rn(p, r, 0x1.555556p-2f);  // 1/3
+    p = __fmaf_rn(p, r, -0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    return __fmaf_rn((float)e, 0x1.62e43p-1f, __fmaf_rn(r, p, t.y));
 }
 
 // cos(2 pi u) for u in (0, 1) a multiple of 2^-24.

@@ -288,14 +288,15 @@ __device__ int kth_action(int kth, const uint16_t* rays, int lane) {
 // virtual N(0,1): Box-Muller on Philox(seed; env, ply, a, TAG_LOGIT) words
 // x, y) and an Exp(1) variate E_a = -ln(word z); the choice is the legal a
 // with the largest q_a / E_a, q_a = e^(z_a - c) (c = 0 for virtual logits,
-// the legal maximum for logits in memory), ties to the smaller action index.
+// the legal maximum for logits in memory), ties to the smaller action index;
+// a beats b when q_a E_b > q_b E_a (two rounded products, no division).
 // That is Gumbel-max: ln(q_a / E_a) = z_a - c + G_a with G_a = -ln E_a
 // Gumbel(0,1), so a is drawn from the softmax of the legal logits.  The
-// log-prob is z_a - c - ln(sum of q over legal actions).  The sum's order is
-// fixed: lane L adds the L-th, (L+32)-th, ... legal action (ascending
-// order) in that order, then a butterfly over the lanes (xor 16, 8, 4, 2,
-// 1); with the float functions above, every value is reproduced bit for bit
-// by the CPU oracle.
+// log-prob is z_a - c - ln(sum of q over legal actions).  The order of the
+// sum and of the comparisons is fixed: lane L takes the L-th, (L+32)-th, ...
+// legal action (ascending order) in that order, then a butterfly over the
+// lanes (xor 16, 8, 4, 2, 1); with the float functions above, every value is
+// reproduced bit for bit by the CPU oracle.
 // acts: the warp's shared-memory scratch (at least 200 bytes).
 // u_pre: the uniform policy's Philox word when the caller drew it already.
 struct Pick {
@@ -348,7 +349,7 @@ __device__ void choose(const Pick& a, const uint16_t* rays, int n, int64_t e, in
     }
     const float* lg = a.logits ? a.logits + e * NACT : nullptr;
     float shift = 0.0f;  // c: 0, or the legal maximum of the logits in memory
-    float best = -1.0f, bestz = 0.0f, s = 0.0f;
+    float bq = 0.0f, bE = 1.0f, bestz = 0.0f, s = 0.0f;  // the lane's best so far: q, E, logit
     int besta = 0x7fffffff;
     // pass 0 (logits in memory only): their legal maximum; pass 1: the choice
 #pragma unroll 1
@@ -373,9 +374,11 @@ __device__ void choose(const Pick& a, const uint16_t* rays, int n, int64_t e, in
             const float z = lg ? lg[ac]
                                : __fmul_rn(__fsqrt_rn(__fmul_rn(-2.0f, xln(unit_open(w.x)))), xcos2pi(unit_open(w.y)));
             const float q = xexp(__fsub_rn(z, shift));
-            const float key = __fdiv_rn(q, -xln(unit_open(w.z)));
-            if (key > best || (key == best && ac < besta)) {
-                best = key;
+            const float E = -xln(unit_open(w.z));
+            const float lhs = __fmul_rn(q, bE), rhs = __fmul_rn(bq, E);
+            if (lhs > rhs || (lhs == rhs && ac < besta)) {
+                bq = q;
+                bE = E;
                 besta = ac;
                 bestz = z;
             }
@@ -390,10 +393,13 @@ __device__ void choose(const Pick& a, const uint16_t* rays, int n, int64_t e, in
     __syncwarp();
 #pragma unroll 1
     for (int o = 16; o; o >>= 1) {
-        const float ob = __shfl_xor_sync(FULL, best, o), oz = __shfl_xor_sync(FULL, bestz, o);
+        const float oq = __shfl_xor_sync(FULL, bq, o), oE = __shfl_xor_sync(FULL, bE, o);
+        const float oz = __shfl_xor_sync(FULL, bestz, o);
         const int oa = __shfl_xor_sync(FULL, besta, o);
-        if (ob > best || (ob == best && oa < besta)) {
-            best = ob;
+        const float lhs = __fmul_rn(oq, bE), rhs = __fmul_rn(bq, oE);
+        if (lhs > rhs || (lhs == rhs && oa < besta)) {
+            bq = oq;
+            bE = oE;
             besta = oa;
             bestz = oz;
         }
