@@ -189,6 +189,7 @@ class StrategoRolloutBuffer:
         self._ply = 0
         self._outs: dict[str, torch.Tensor] | None = None
         self._host: dict | None = None
+        self._pol_cache: dict = {}
 
     # ------------------------------------------------------------------
     # plumbing
@@ -442,31 +443,44 @@ class StrategoRolloutBuffer:
         """Device status bits (SB_STATUS_*) raised since construction."""
         return int(self._status.item())
 
+    def _alloc_outputs(self, stats: torch.Tensor | None) -> dict[str, torch.Tensor]:
+        n, dev = self._n, self.device
+        chans = NUM_CHANNELS if self.obs_layout == "dense" else COMPACT_CHANNELS
+        # reward, next_action and done share one block (see _results_layout) so
+        # that step_host brings all three back with a single copy.
+        lay = _results_layout(n)
+        res = torch.zeros(lay["bytes"], dtype=torch.uint8, device=dev)
+        o: dict = {
+            "infostate": torch.zeros((n, chans, 10, 10), dtype=self.obs_dtype, device=dev),
+            "results": res,
+            "reward": _results_view(res, lay, "reward", n),
+            "done": _results_view(res, lay, "done", n),
+            "action": torch.zeros(n, dtype=torch.int64, device=dev),
+            "logprob": torch.zeros(n, dtype=torch.float32, device=dev),
+            "next_action": _results_view(res, lay, "next_action", n),
+            "next_logprob": torch.zeros(n, dtype=torch.float32, device=dev),
+            "stats": torch.zeros(5, dtype=torch.int64, device=dev) if stats is None else stats,
+        }
+        if self.mask_format == "u8":
+            o["mask"] = torch.zeros((n, NUM_SQUARES, NUM_SQUARES), dtype=torch.uint8, device=dev)
+        elif self.mask_format == "bits":
+            o["mask"] = torch.zeros((n, MASK_BITS_BYTES), dtype=torch.uint8, device=dev)
+        o["_args"] = {}  # prebuilt ctypes arguments of step(), per observe flag
+        return o
+
     def _ensure_outputs(self) -> dict[str, torch.Tensor]:
         if self._outs is None:
-            n, dev = self._n, self.device
-            chans = NUM_CHANNELS if self.obs_layout == "dense" else COMPACT_CHANNELS
-            # reward, next_action and done share one block (see _results_layout) so
-            # that step_host brings all three back with a single copy.
-            lay = _results_layout(n)
-            res = torch.zeros(lay["bytes"], dtype=torch.uint8, device=dev)
-            o: dict[str, torch.Tensor] = {
-                "infostate": torch.zeros((n, chans, 10, 10), dtype=self.obs_dtype, device=dev),
-                "results": res,
-                "reward": _results_view(res, lay, "reward", n),
-                "done": _results_view(res, lay, "done", n),
-                "action": torch.zeros(n, dtype=torch.int64, device=dev),
-                "logprob": torch.zeros(n, dtype=torch.float32, device=dev),
-                "next_action": _results_view(res, lay, "next_action", n),
-                "next_logprob": torch.zeros(n, dtype=torch.float32, device=dev),
-                "stats": torch.zeros(5, dtype=torch.int64, device=dev),
-            }
-            if self.mask_format == "u8":
-                o["mask"] = torch.zeros((n, NUM_SQUARES, NUM_SQUARES), dtype=torch.uint8, device=dev)
-            elif self.mask_format == "bits":
-                o["mask"] = torch.zeros((n, MASK_BITS_BYTES), dtype=torch.uint8, device=dev)
-            self._outs = o
+            self._outs = self._alloc_outputs(None)
         return self._outs
+
+    def new_outputs(self) -> dict[str, torch.Tensor]:
+        """A further set of step outputs for ``step(outputs=...)``: infostate,
+        legal mask and per-game results laid out as the buffer's own (their
+        zero infostate planes written once, here).  With two or more sets a
+        consumer can read one ply's observations while the next ply writes
+        another set.  The episode statistics stay shared with the buffer's
+        own outputs."""
+        return self._alloc_outputs(self._ensure_outputs()["stats"])
 
     def _policy(self, policy: str, logits: torch.Tensor | None) -> C.SbPolicy:
         if policy not in _POLICIES:
@@ -505,6 +519,7 @@ class StrategoRolloutBuffer:
         logits: torch.Tensor | None = None,
         auto_reset: bool = True,
         observe: bool = True,
+        outputs: dict | None = None,
     ) -> StepOutput:
         """One ply for every game, fused in one kernel.
 
@@ -513,10 +528,33 @@ class StrategoRolloutBuffer:
         [N,10000] float32 for 'gumbel', else virtual Philox N(0,1) logits).
         Then: apply, per-game auto-reset from the setup pool for games that
         ended, and the legal mask / infostate of the new state into the
-        buffer's persistent outputs.  The returned tensors are views of those
-        outputs and are overwritten by the next step.
+        buffer's persistent outputs (or into ``outputs``, a set made by
+        :meth:`new_outputs`).  The returned tensors are views of those outputs
+        and are overwritten by the next step that writes the same set.
         """
-        o = self._ensure_outputs()
+        o = self._ensure_outputs() if outputs is None else outputs
+        if logits is None and actions is None and self._n:
+            # the common device-sampled step: one native call on prebuilt arguments
+            args = o["_args"].get(observe)
+            if args is None:
+                args = o["_args"][observe] = (ctypes.byref(self._step_out(o, observe)),
+                                              self._step_views(o, observe))
+            pol = self._pol_cache.get(policy)
+            if pol is None:
+                pol = self._pol_cache[policy] = ctypes.byref(self._policy(policy, None))
+            dev = self._device_id
+            fn = C.lib().sb_step
+            if torch.cuda.current_device() != dev:
+                with torch.cuda.device(self.device):
+                    rc = fn(ctypes.byref(self._st), None, self._ply, pol, 1 if auto_reset else 0, args[0],
+                            _raw_stream(dev))
+            else:
+                rc = fn(ctypes.byref(self._st), None, self._ply, pol, 1 if auto_reset else 0, args[0],
+                        _raw_stream(dev))
+            if rc:
+                C.check(rc)
+            self._ply += 1
+            return args[1]
         self.step_raw(actions, policy=policy, logits=logits, auto_reset=auto_reset,
                       outputs=self._step_out(o, observe))
         return self._step_views(o, observe)

@@ -2131,6 +2131,20 @@ int sb_step_host_noalloc(const sb_state* s, const sb_host_io* io, int64_t ply, c
     if (io->actions_dev) return fail(SB_E_ARG, "actions_dev must be NULL: the library stages the actions itself");
     if (s->n > SB_NOALLOC_MAX_ENVS)
         return fail(SB_E_ARG, "%lld envs: at most %d per call without allocation", (long long)s->n, SB_NOALLOC_MAX_ENVS);
+    if (s->n > 0 && io->actions_host) {
+        // the staging array used is the current device's: the games must live there
+        int dev = 0;
+        cudaPointerAttributes at;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+        e = cudaPointerGetAttributes(&at, s->records);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return fail(SB_E_ARG, "records are not device memory");
+        }
+        if (at.type != cudaMemoryTypeDevice || at.device != dev)
+            return fail(SB_E_ARG, "records live on device %d, but device %d is current", at.device, dev);
+    }
     sb_host_io local = *io;
     if (io->actions_host && (rc = noalloc_staging(&local.actions_dev)) != SB_OK) return rc;
     return sb_step_host(s, &local, ply, policy, auto_reset, out, stream);

@@ -12,14 +12,20 @@ every ply rewrites the 75 live channels), uint8 mask [B,100,100].  One step =
 one ply over all envs = one launch of the fused step kernel.  Synthetic data:
 there is no dataset; setups and actions come from Philox.
 
-Timing: W untimed warm-up steps; then K steps, each bracketed by CUDA events
-on the buffer's stream, with a 512 MiB write and a 256 MiB read between timed
-steps to flush the 126 MB L2 (outside the bracketed interval); barrier +
-synchronize on both
-sides; max over ranks.  Multi-GPU (torchrun): each rank owns its own 4096 envs
-(global env indices rank*4096 ...), no collective on the step path (weak
-scaling); an NCCL all-gather of the episode statistics follows the timed
-region.
+Timing (config 2, default ``--timing graph``): W untimed warm-up steps, then
+the K timed steps, launched back to back as one CUDA graph (captured after the
+warm-up, each node one fused-step launch with its own ply number) and
+replayed once between two CUDA events on the buffer's stream; barrier +
+synchronize on both sides; max over ranks.  The steps write their outputs
+into 4 output sets in turn (4 x 441 MB, 14x the 126 MB L2), so no step
+writes lines still held in L2 and every step's 104.6 MB of writes reaches
+HBM inside the timed region (the game records, 1 MB, stay in L2 from ply to
+ply, as in any rollout).  ``--timing flush`` is the per-launch form: each
+step bracketed by its own events, with a 512 MiB write and a 256 MiB read
+between steps (outside the bracketed interval) to flush L2.
+Multi-GPU (torchrun): each rank owns its own 4096 envs (global env indices
+rank*4096 ...), no collective on the step path (weak scaling); an NCCL
+all-gather of the episode statistics follows the timed region.
 
 e2e: the same steps through the public host API (``step_host``: int64 actions
 from page-locked host memory in, reward / done / next action back into
@@ -30,6 +36,13 @@ around the loop; ``--e2e-api serve`` uses the persistent step server instead.
 host cores: the C restatement in oracle/ (the reference's own code is Python
 and cannot run on the GPU box), same config (the 4096-game batch per step),
 all host threads; under torchrun rank 0 alone runs it.
+
+``--impl reference-cuda`` times the reference's own CUDA kernels
+(csrc/stratego_buffer.cu compiled from its source into oracle/_ref/, driven as
+its pybind class drives them: apply_actions with its flag-count reductions,
+then compute_legal_action_mask and compute_infostate_tensor, each a zeroed
+fresh output plus a kernel) at config 2's 4096 games per ply, on the same
+games and actions as this build's step.
 """
 
 from __future__ import annotations
@@ -63,6 +76,7 @@ METRIC = "env state updates/sec (step+mask+infostate)"
 #   next logprob f32 .................. 23
 # (chase-ring reads on threatening moves and pool reads on resets are left out.)
 BYTES_PER_UPDATE = 256 + 256 + 10_000 + 15_000 + 23
+NUM_CH_DENSE = 488
 
 
 def _peaks() -> tuple[float, str]:
@@ -205,6 +219,68 @@ def run_reference(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_reference_cuda(args, rank: int) -> None:
+    """The reference's own CUDA kernels at config 2 (rank 0 only): per ply,
+    apply_actions + compute_legal_action_mask + compute_infostate_tensor of
+    the reference class (oracle/refcuda.py), on the games and actions this
+    build's step plays from the same setups (without auto-reset: the
+    reference class resets only from caller-supplied planes)."""
+    if rank != 0:
+        return
+    from oracle import refcuda
+
+    if not refcuda.available():
+        print(json.dumps({"impl": "reference-cuda", "unavailable": "oracle/_ref/libref_stratego_cuda.so was not "
+                          "built (it is compiled where the reference checkout is present)"}), flush=True)
+        return
+    from ataraxos_b200 import StrategoRolloutBuffer
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    B, W, K = args.envs, args.warmup, args.steps
+    ours = StrategoRolloutBuffer(B, dev.index, seed=SEED, pool_size=POOL, pool_seed=SEED, obs_layout="compact",
+                                 mask_format="none")
+    ours.reset_all_from_pool()
+    ow, pc = ours.get_board_owner(), ours.get_board_piece()
+    red = torch.where(ow == 0, pc, torch.zeros_like(pc))
+    blue = torch.where(ow == 1, pc, torch.zeros_like(pc))
+    acts = torch.empty((W + K, B), dtype=torch.int64, device=dev)
+    for t in range(W + K):
+        acts[t].copy_(ours.step(None, auto_reset=False, observe=False).action)
+    ref = refcuda.RefCudaBuffer(B, dev.index)
+    ref.reset_all(red, blue)
+
+    def ply(t):
+        ref.apply_actions(acts[t])
+        ref.compute_legal_action_mask()
+        ref.compute_infostate_tensor()
+
+    for t in range(W):
+        ply(t)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for t in range(W, W + K):
+        ply(t)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    value = B * K / (ms / 1e3)
+    bpu = 2 * (NUM_CH_DENSE * 100 * 4 + 10_000)  # zero fill + kernel write of the f32 infostate and bool mask
+    peak, _ = _peaks()
+    print(json.dumps({
+        "impl": "reference-cuda", "metric": METRIC, "value": value, "unit": "updates/s", "n_gpus": 1, "steps": K,
+        "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
+        "config": {"workload": f"config2: {B} envs, reference kernels (csrc/stratego_buffer.cu, -O3 --use_fast_math, "
+                               "sm_100a) driven as its pybind class drives them; f32 [B,488,10,10] infostate + bool "
+                               "[B,100,100] mask per ply, each zero-filled then written",
+                   "l2": "outputs of one ply (841 MB) exceed L2; no flush"},
+        "roofline": {"bound": "hbm", "bytes_per_update": bpu, "achieved": bpu * B / (ms / K / 1e3) / 1e9,
+                     "peak": peak, "unit": "GB/s"},
+        "gpu_launches": None,
+    }), flush=True)
+
+
 def _profile_traffic(name: str, updates_per_launch: int | None = None) -> float | None:
     """DRAM bytes (read + write) per launch from the ncu capture summarised in
     profiles/<name>: its dram_bytes_per_launch, or, for a capture taken on a
@@ -250,6 +326,30 @@ class Ctx:
         return sharding.gather_episode_stats(stats).sum(0).tolist()
 
 
+def timed_graph(ctx: Ctx, launch, first: int, k: int):
+    """launch(first) .. launch(first + k - 1) captured into one CUDA graph,
+    then replayed once between CUDA events (no host work between steps)."""
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(first, first + k):
+            launch(i)
+    torch.cuda.synchronize(ctx.dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx.barrier()
+    torch.cuda.synchronize(ctx.dev)
+    torch.cuda.nvtx.range_push("timed")
+    with ClockSampler(ctx.dev) as clocks:
+        e0.record(ctx.stream)
+        g.replay()
+        e1.record(ctx.stream)
+        torch.cuda.synchronize(ctx.dev)
+        ctx.barrier()
+    torch.cuda.nvtx.range_pop()
+    total_ms = ctx.max_over_ranks(e0.elapsed_time(e1))
+    del g
+    return total_ms, clocks.summary()
+
+
 def timed_launches(ctx: Ctx, launch, k: int, flush_mib: int):
     """k launches, each bracketed by CUDA events; L2 flushed between them when flush_mib > 0."""
     flush = flush_rd = None
@@ -285,11 +385,12 @@ def e2e_loop(ctx: Ctx, buf, steps: int, policy: str = "uniform", total_envs: int
     (int64[B], page-locked host memory) cross to the device, the fused step
     runs, and reward, done and the next proposed actions cross back into
     page-locked host memory; the host takes the proposals as its next actions.
-    Uniform steps go through the persistent step server
-    (``StrategoRolloutBuffer.serve``: no launch or stream synchronisation per
-    step, CUDA events around the server kernel's whole life); otherwise
-    ``step_host`` (the kernel reads / writes the page-locked memory in place,
-    CUDA events around the loop).  Returns (updates/s, h2d, d2h bytes, api)."""
+    By default (``--e2e-api step_host``) every step is one ``step_host`` call
+    (the kernel reads / writes the page-locked memory in place, CUDA events
+    around the loop).  ``--e2e-api serve`` runs uniform steps through the
+    persistent step server instead (``StrategoRolloutBuffer.serve``: no launch
+    or stream synchronisation per step, CUDA events around the server
+    kernel's whole life).  Returns (updates/s, h2d, d2h bytes, api)."""
     from ataraxos_b200.serve import StepServer
 
     B = buf.n_games
@@ -346,10 +447,20 @@ def run_step_config(ctx: Ctx, cfg: int) -> dict:
     buf = StrategoRolloutBuffer(B, ctx.local, seed=SEED, env_base=env_base, pool_size=pool, pool_seed=SEED,
                                 obs_dtype=torch.bfloat16, obs_layout="dense", mask_format="u8")
     buf.reset_all_from_pool()
-    for _ in range(a.warmup):
-        buf.step(None, policy=policy)
-    flush = a.flush_mib if cfg == 2 else 0  # config 3 writes 6.7 GB/GPU per step: far above L2
-    total_ms, clocks = timed_launches(ctx, lambda i: buf.step(None, policy=policy), a.steps, flush)
+    graph = cfg == 2 and a.timing == "graph"
+    # config 2 under graph timing: the steps write 4 output sets in turn (see the module docstring)
+    sets = [buf._ensure_outputs()] + [buf.new_outputs() for _ in range(3)] if graph else [None]
+
+    def launch(i):
+        buf.step(None, policy=policy, outputs=sets[i % len(sets)])
+
+    for i in range(a.warmup):
+        launch(i)
+    if graph:
+        total_ms, clocks = timed_graph(ctx, launch, a.warmup, a.steps)
+    else:
+        flush = a.flush_mib if cfg == 2 else 0  # config 3 writes 6.7 GB/GPU per step: far above L2
+        total_ms, clocks = timed_launches(ctx, launch, a.steps, flush)
     launch_ms = total_ms / a.steps
     stats = ctx.gather_stats(buf.episode_stats().clone())
     if cfg == 2:
@@ -357,7 +468,12 @@ def run_step_config(ctx: Ctx, cfg: int) -> dict:
         workload = (f"config2: {B} envs/GPU, seeded random setups (pool {pool}), uniform random legal actions, "
                     "auto-reset, bf16 [B,488,10,10] infostate (75 live planes rewritten per ply), u8 [B,100,100] "
                     "mask; one step = one fused-kernel ply over all envs")
-        l2 = f"flushed between timed steps ({a.flush_mib} MiB write, then {a.flush_mib // 2} MiB read)"
+        if graph:
+            l2 = ("back-to-back steps (one CUDA graph of the K timed launches); outputs written to 4 sets in turn "
+                  "(4 x 441 MB, 14x L2): no step rewrites lines held in L2, every step's writes reach HBM in the "
+                  "timed region")
+        else:
+            l2 = f"flushed between timed steps ({a.flush_mib} MiB write, then {a.flush_mib // 2} MiB read)"
         scaling = "weak"
     else:
         e2e, h2d, d2h, api = e2e_loop(ctx, buf, max(10, a.e2e_steps // 10), policy, total)
@@ -492,7 +608,7 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--impl", choices=["b200", "reference", "reference-cuda"], default="b200")
     ap.add_argument("--config", type=int, choices=[2, 3, 4, 5], default=2)
     ap.add_argument("--envs", type=int, default=4096, help="envs per GPU (config 2)")
     ap.add_argument("--plies-per-launch", type=int, default=8, help="config 4 rollout launch length")
@@ -503,6 +619,9 @@ def main() -> None:
                     help="host API of the e2e loop: the persistent step server or step_host")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--flush-mib", type=int, default=512)
+    ap.add_argument("--timing", choices=["graph", "flush"], default="graph",
+                    help="config 2: K back-to-back steps as one CUDA graph over 4 output sets, or per-launch events "
+                         "with an L2 flush between launches")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = {2: 3000, 3: 100, 4: 40, 5: 10}[args.config]
@@ -510,6 +629,9 @@ def main() -> None:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args, int(os.environ.get("RANK", "0")))
+        return
+    if args.impl == "reference-cuda":
+        run_reference_cuda(args, int(os.environ.get("RANK", "0")))
         return
 
     ctx = Ctx(args)

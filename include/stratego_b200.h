@@ -191,9 +191,14 @@ int sb_step_host(const sb_state *s, const sb_host_io *io, int64_t ply, const sb_
  * by every GPU that loads the library until the process exits); pageable or
  * page-locked host memory both work.  io->actions_dev must be NULL; every
  * other io field means what it does for sb_step_host.  Calls with more than
- * SB_NOALLOC_MAX_ENVS envs return SB_E_ARG.  The first call on a device looks
- * up the array's device address (cudaGetSymbolAddress) with that device
- * current; make that first call before any stream capture.  Every call on a
+ * SB_NOALLOC_MAX_ENVS envs return SB_E_ARG, and so do calls whose records do
+ * not live on the current device (the array used is the current device's).
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current and keeps it until the
+ * process exits; make that first call before any stream capture.  A
+ * cudaDeviceReset (or anything else that tears down the device's primary
+ * context) invalidates the kept address: do not call this entry point after
+ * one.  Every call on a
  * device shares the one array: calls that overlap on the GPU (on different
  * streams) race on it.  Each call overwrites the entries it reads, so nothing
  * needs clearing between calls.  Nothing is allocated. */

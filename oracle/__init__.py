@@ -82,6 +82,7 @@ class _OConfig(ctypes.Structure):
         ("env_base", ctypes.c_int64),
         ("pool", ctypes.c_void_p),
         ("pool_size", ctypes.c_int64),
+        ("genv", ctypes.c_void_p),
     ]
 
 
@@ -112,6 +113,9 @@ def lib() -> ctypes.CDLL:
             "or_sample": (None, [S, C, i64, i32, vp, vp, vp]),
             "or_step": (None, [S, C, vp, i64, i32, i32, vp, vp, vp, vp]),
             "or_bench_rollout": (ctypes.c_int, [S, C, i64, i64, i32, vp, vp]),
+            "or_run": (ctypes.c_int, [S, C, i64, i64, i32, i32, i32, vp, vp, vp, vp]),
+            "or_observe": (ctypes.c_int, [S, C, i32, vp, vp, vp, i32]),
+            "or_virtual_logits": (None, [S, C, i64, i32, vp, vp, vp]),
             "or_fraction": (ctypes.c_float, [ctypes.c_int32, ctypes.c_int32]),
             "or_belief_resample": (None, [S, S, vp, C]),
             "or_f32_to_bf16": (ctypes.c_uint16, [ctypes.c_float]),
@@ -214,7 +218,11 @@ class OracleState:
         zobrist: np.ndarray | None = None,
         pool: np.ndarray | None = None,
         rules: int = RULES_CUDA,
+        genv: np.ndarray | None = None,
     ) -> None:
+        """``genv``: the global index of each env, for replaying a subsample
+        of a larger batch (each env's Philox streams are keyed by it); by
+        default env g is ``env_base + g``."""
         if rules == RULES_ISF and not 1 <= two_square_limit <= 3:
             raise ValueError("the ISF two-square tracker supports limits 1..3")
         self.n = int(n)
@@ -228,7 +236,9 @@ class OracleState:
                            **{_CFIELD[k]: _ptr(v) for k, v in self.a.items()})
         self.zobrist = np.ascontiguousarray(zobrist_table() if zobrist is None else zobrist, dtype=np.int64)
         self.pool = None if pool is None else np.ascontiguousarray(pool, dtype=np.uint8)
+        self.genv = None if genv is None else np.ascontiguousarray(genv, dtype=np.int64).reshape(self.n)
         self._cfg = _OConfig(
+            genv=_ptr(self.genv),
             zobrist=_ptr(self.zobrist),
             no_attack_limit=no_attack_limit,
             max_game_length=max_game_length,
@@ -317,6 +327,58 @@ class OracleState:
         )
         self.ply += 1
         return {"action": taken, "logprob": lp, "reward": rew, "done": done}
+
+    def run(self, plies: int, *, policy: int = POLICY_UNIFORM, auto_reset: bool = True, threads: int | None = None,
+            record: bool = True) -> dict[str, np.ndarray] | None:
+        """``plies`` calls of :meth:`step` with sampled actions, on ``threads``
+        host threads (default: all); with ``record`` the per-ply taken action,
+        log-prob, reward and done come back as ``[plies, n]`` arrays."""
+        threads = threads or os.cpu_count() or 1
+        out = None
+        if record:
+            out = {"action": np.empty((plies, self.n), np.int64), "logprob": np.empty((plies, self.n), np.float32),
+                   "reward": np.empty((plies, self.n), np.float32), "done": np.empty((plies, self.n), np.uint8)}
+        o = out or {}
+        rc = lib().or_run(ctypes.byref(self._st), ctypes.byref(self._cfg), plies, self.ply, policy, int(auto_reset),
+                          threads, _ptr(o.get("action")), _ptr(o.get("logprob")), _ptr(o.get("reward")),
+                          _ptr(o.get("done")))
+        if rc != 0:
+            raise RuntimeError("oracle run failed to start its threads")
+        self.ply += plies
+        return out
+
+    def observe(self, *, mask_u8: bool = False, mask_bits: bool = False, info: str | None = None,
+                threads: int | None = None) -> dict[str, np.ndarray]:
+        """Observations of the current state on ``threads`` host threads:
+        ``mask_u8`` [n,100,100], ``mask_bits`` [n,1250], and ``info`` "dense"
+        (bf16 bits [n,488,10,10]) or "compact" (bf16 bits [n,76,10,10]:
+        planes 0-42, a zero pad, 456-487)."""
+        threads = threads or os.cpu_count() or 1
+        out: dict[str, np.ndarray] = {}
+        if mask_u8:
+            out["mask_u8"] = np.empty((self.n, NSQ, NSQ), np.uint8)
+        if mask_bits:
+            out["mask_bits"] = np.empty((self.n, NACT // 8), np.uint8)
+        if info is not None:
+            if info not in ("dense", "compact"):
+                raise ValueError("info must be 'dense' or 'compact'")
+            out["info"] = np.empty((self.n, NCH if info == "dense" else 76, 10, 10), np.uint16)
+        rc = lib().or_observe(ctypes.byref(self._st), ctypes.byref(self._cfg), threads, _ptr(out.get("mask_u8")),
+                              _ptr(out.get("mask_bits")), _ptr(out.get("info")), int(info == "compact"))
+        if rc != 0:
+            raise RuntimeError("oracle observe failed to start its threads")
+        return out
+
+    def virtual_logits(self, ply: int, cap: int = 256) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+        """The Gumbel sampler's virtual N(0,1) logits at ``ply``: per env its
+        legal actions (ascending) ``[n, cap]`` int16, their logits ``[n, cap]``
+        float32 and the legal-move counts ``[n]``."""
+        acts = np.full((self.n, cap), -1, np.int16)
+        z = np.full((self.n, cap), np.nan, np.float32)
+        cnt = np.empty(self.n, np.int32)
+        lib().or_virtual_logits(ctypes.byref(self._st), ctypes.byref(self._cfg), ply, cap, _ptr(acts), _ptr(z),
+                                _ptr(cnt))
+        return acts, z, cnt
 
     def resample_from(self, roots: "OracleState", root_of) -> None:
         """Belief resampling: env j becomes root root_of[j] re-dealt (see stratego_oracle.c)."""

@@ -42,6 +42,7 @@ arrays for a few envs.
 from __future__ import annotations
 
 import argparse
+import os
 import hashlib
 import sys
 from pathlib import Path
@@ -344,7 +345,9 @@ class _Ref:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("ATARAXOS_REFERENCE"),
+                    required="ATARAXOS_REFERENCE" not in os.environ,
+                    help="checkout of the reference project (or set ATARAXOS_REFERENCE)")
     args = ap.parse_args()
     ref = _Ref(Path(args.reference))
 

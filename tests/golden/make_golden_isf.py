@@ -31,6 +31,7 @@ once the game is over) and, per ply, whether the move violated each rule.
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 from pathlib import Path
 
@@ -143,7 +144,9 @@ class _Ref:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("ATARAXOS_REFERENCE"),
+                    required="ATARAXOS_REFERENCE" not in os.environ,
+                    help="checkout of the reference project (or set ATARAXOS_REFERENCE)")
     args = ap.parse_args()
     R = _Ref(Path(args.reference))
     rng = np.random.default_rng(20251201)

@@ -22,18 +22,18 @@ from _helpers import assert_state_equal, export_np
 pytestmark = pytest.mark.gpu
 
 
-def _twins(n, seed):
+def _twins(n, seed, **kw):
     from ataraxos_b200 import StrategoRolloutBuffer
 
     pool = torch.from_numpy(oracle.make_setup_pool(seed, 512))
-    a = StrategoRolloutBuffer(n, 0, seed=seed, setup_pool=pool, no_attack_limit=30)
-    b = StrategoRolloutBuffer(n, 0, seed=seed, setup_pool=pool, no_attack_limit=30)
+    a = StrategoRolloutBuffer(n, 0, seed=seed, setup_pool=pool, no_attack_limit=30, **kw)
+    b = StrategoRolloutBuffer(n, 0, seed=seed, setup_pool=pool, no_attack_limit=30, **kw)
     a.reset_all_from_pool()
     b.reset_all_from_pool()
     return a, b
 
 
-def _noalloc_step(buf, actions):
+def _noalloc_step(buf, actions, observe=True):
     """One ply of ``buf`` through sb_step_host_noalloc: ``actions`` is a CPU
     int64 array (pageable or page-locked) or None; reward / done /
     next_action come back into the buffer's page-locked result block."""
@@ -45,10 +45,10 @@ def _noalloc_step(buf, actions):
                     back_dev=cp.back_dev, back_host=cp.back_host, back_bytes=cp.back_bytes, sync=1, reserved=0)
     pol = C.SbPolicy(kind=C.SB_POLICY_UNIFORM, reserved=0, logits=None)
     rc = C.lib().sb_step_host_noalloc(ctypes.byref(buf._st), ctypes.byref(io), buf.ply, ctypes.byref(pol), 1,
-                                      h["out"]["copy"][True], torch.cuda.current_stream().cuda_stream)
+                                      h["out"]["copy"][observe], torch.cuda.current_stream().cuda_stream)
     assert rc == 0, C.lib().sb_last_error()
     buf._ply += 1
-    return h["ret"]["copy"][True]
+    return h["ret"]["copy"][observe]
 
 
 def _same(r, ref, t):
@@ -111,3 +111,24 @@ def test_noalloc_refuses_before_launch():
     assert_state_equal(export_np(a), export_np(b), "after refusals")
     ra, rb = _noalloc_step(a, None), b.step_host(None, mapped=False)
     _same(ra, rb, "after refusals")
+
+
+def test_noalloc_full_staging_array():
+    """A shard of exactly SB_NOALLOC_MAX_ENVS games fills the staging array:
+    accepted, and equal to sb_step_host on a twin buffer."""
+    import ataraxos_b200._capi as C
+
+    n = C.SB_NOALLOC_MAX_ENVS
+    a, b = _twins(n, 31, obs_layout="compact", mask_format="none")
+    acts = b.step_host(None, mapped=False, observe=False).next_action.to(torch.int64)
+    _noalloc_step(a, None, observe=False)
+    acts[::7] = 0  # illegal for those games: ignored and counted
+    for t in range(3):
+        r_ref = b.step_host(acts, mapped=False, observe=False)
+        r = _noalloc_step(a, acts, observe=False)
+        np.testing.assert_array_equal(r.reward.numpy(), r_ref.reward.numpy(), err_msg=f"ply {t}")
+        np.testing.assert_array_equal(r.done.numpy(), r_ref.done.numpy(), err_msg=f"ply {t}")
+        np.testing.assert_array_equal(r.next_action.numpy(), r_ref.next_action.numpy(), err_msg=f"ply {t}")
+        acts = r.next_action.to(torch.int64)
+    assert torch.equal(a._records, b._records)
+    assert a.status() == 0
