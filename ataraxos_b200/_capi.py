@@ -7,9 +7,15 @@ entry point raises.  Build it with ``python -m ataraxos_b200.build``.
 from __future__ import annotations
 
 import ctypes
+import os
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libstratego_b200.so"
+_LIB_DIR = Path(__file__).resolve().parent / "_lib"
+# ATARAXOS_B200_DEBUG=1 selects the debug build, whose kernels check every game
+# record's indices first and skip a bad game (SB_STATUS_BAD_STATE) instead of
+# reading or writing out of range; it is slower and meant for loaded records.
+DEBUG = os.environ.get("ATARAXOS_B200_DEBUG", "0") not in ("", "0")
+LIB_PATH = _LIB_DIR / ("libstratego_b200_debug.so" if DEBUG else "libstratego_b200.so")
 
 SB_OK, SB_E_ARG, SB_E_CUDA, SB_E_NOPOOL = 0, -1, -2, -3
 SB_DTYPE_F32, SB_DTYPE_BF16 = 0, 1
@@ -19,6 +25,7 @@ SB_RULES_CUDA, SB_RULES_ISF = 0, 1
 SB_NOALLOC_MAX_ENVS = 262144
 SB_STATUS_BAD_SETUP = 1
 SB_STATUS_WAIT_TIMEOUT = 2
+SB_STATUS_BAD_STATE = 4
 RECORD_BYTES = 256
 ISF_TS_BYTES = 600  # per env under SB_RULES_ISF: 100 squares x 3 intervals x (lo, hi)
 
@@ -118,6 +125,7 @@ class SbHostIo(ctypes.Structure):
 _SIGS = {
     "sb_abi_version": (ctypes.c_int, []),
     "sb_last_error": (ctypes.c_char_p, []),
+    "sb_debug_bounds": (ctypes.c_int, []),
     "sb_init_state": (ctypes.c_int, [ctypes.POINTER(SbState), vp]),
     "sb_hello_world": (ctypes.c_int, [vp, vp]),
     "sb_reset_planes": (ctypes.c_int, [ctypes.POINTER(SbState), vp, vp, ctypes.c_int, vp]),

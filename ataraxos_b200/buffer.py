@@ -105,7 +105,7 @@ class StepOutput:
     done: torch.Tensor               # [N] bool, the transition ended the game
     action: torch.Tensor             # [N] int64, action applied (-1 none)
     logprob: torch.Tensor            # [N] float32, log-prob of the applied action when sampled
-    next_action: torch.Tensor        # [N] int16, action proposed for the new state
+    next_action: torch.Tensor        # [N] int16, action proposed for the new state (-1: none, game over)
     next_logprob: torch.Tensor       # [N] float32
 
 
@@ -116,7 +116,7 @@ class HostStepOutput:
 
     reward: torch.Tensor       # [N] float32, player-0 reward of the transition
     done: torch.Tensor         # [N] bool
-    next_action: torch.Tensor  # [N] int16, action proposed for the new state
+    next_action: torch.Tensor  # [N] int16, action proposed for the new state (-1: none, game over)
     device: StepOutput
 
 

@@ -18,6 +18,8 @@ CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 LIB_DIR = PKG / "_lib"
 LIB_PATH = LIB_DIR / "libstratego_b200.so"
+# the debug build: every kernel checks each game record's indices first (SB_DEBUG_BOUNDS)
+DEBUG_LIB_PATH = LIB_DIR / "libstratego_b200_debug.so"
 SOURCES = [CSRC / "sb_kernels.cu"]
 DEPS = SOURCES + [CSRC / "sb_device.cuh", INCLUDE / "stratego_b200.h"]
 
@@ -35,24 +37,30 @@ def nvcc() -> str:
     raise FileNotFoundError("nvcc not found: the CUDA toolkit is needed to build libstratego_b200.so")
 
 
-def up_to_date() -> bool:
-    if not LIB_PATH.exists():
+def up_to_date(path: Path = LIB_PATH) -> bool:
+    if not path.exists():
         return False
-    t = LIB_PATH.stat().st_mtime
+    t = path.stat().st_mtime
     return all(d.stat().st_mtime <= t for d in DEPS)
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and up_to_date():
-        return LIB_PATH
+def _compile(path: Path, extra: list[str], verbose: bool) -> None:
     LIB_DIR.mkdir(exist_ok=True)
-    tmp = LIB_PATH.with_name(f".{LIB_PATH.name}.{os.getpid()}.tmp")
-    cmd = [nvcc(), *NVCC_FLAGS, f"-I{INCLUDE}", "-o", str(tmp), *map(str, SOURCES)]
+    tmp = path.with_name(f".{path.name}.{os.getpid()}.tmp")
+    cmd = [nvcc(), *NVCC_FLAGS, *extra, f"-I{INCLUDE}", "-o", str(tmp), *map(str, SOURCES)]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)
-    os.replace(tmp, LIB_PATH)
+    os.replace(tmp, path)
+
+
+def build(force: bool = False, verbose: bool = False, debug: bool = True) -> Path:
+    """Build the production library (and, with ``debug``, the bounds-checking one)."""
+    if force or not up_to_date(LIB_PATH):
+        _compile(LIB_PATH, [], verbose)
+    if debug and (force or not up_to_date(DEBUG_LIB_PATH)):
+        _compile(DEBUG_LIB_PATH, ["-DSB_DEBUG_BOUNDS"], verbose)
     return LIB_PATH
 
 

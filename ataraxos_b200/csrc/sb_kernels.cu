@@ -1080,6 +1080,60 @@ __device__ void write_mask_bits(const uint32_t* w, int lane, uint8_t* g) {
 }
 
 // ---------------------------------------------------------------------------
+// Debug build: bounds checks of a game record
+// ---------------------------------------------------------------------------
+//
+// Built with -DSB_DEBUG_BOUNDS (libstratego_b200_debug.so), every kernel that
+// plays or observes a game first checks that the record holds nothing the
+// kernels would use as an out-of-range index: piece codes (they index the
+// Zobrist table), the side to move, the history ring's head / length and its
+// live entries (square indices of the history planes), the chase rings'
+// heads / lengths, the two-square pair squares and the cached proposal.  A
+// record that fails is left untouched and its game skipped for the launch,
+// and SB_STATUS_BAD_STATE is raised; nothing traps.  Records written only by
+// these kernels always pass; the checks are for records a caller loaded.
+#ifdef SB_DEBUG_BOUNDS
+constexpr bool kDebugBounds = true;
+#else
+constexpr bool kDebugBounds = false;
+#endif
+
+__device__ bool record_ok(const uint8_t* rec, int lane, int rules) {
+    bool ok = true;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int sq = lane + 32 * k;
+        if (sq < NSQ) {
+            const uint8_t c = rec[sq];
+            const int pc = c & C_PIECE;
+            ok &= (c & C_OCC) ? (pc >= 1 && pc <= 12) : (c & (C_PIECE | C_BLUE)) == 0;
+        }
+    }
+    const int hh = rec[R_HHEAD], hl = rec[R_HLEN];
+    if (lane < hl && hl <= NHIST) {
+        const int act = fld<int16_t>(rec, R_HIST + 2 * ((hh - 1 - lane) & 31));
+        ok &= act >= 0 && act < NACT;
+    }
+    if (lane == 0) {
+        const int p = fld<int8_t>(rec, R_PLAYER), oc = fld<int8_t>(rec, R_OUTCOME);
+        ok &= (p == 0 || p == 1) && oc >= -1 && oc <= 2 && rec[R_TERM] <= 1;
+        ok &= hh < NHIST && hl <= NHIST;
+        for (int q = 0; q < 2; ++q) {
+            ok &= rec[R_CHHEAD + q] < NRING && rec[R_CHLEN + q] <= NRING;
+            const int last = fld<int8_t>(rec, R_CHLAST + q);
+            ok &= last >= -1 && last < NSQ;
+            if (rules == SB_RULES_CUDA) {
+                const int lo = fld<int16_t>(rec, R_TSLO + 2 * q), hi = fld<int16_t>(rec, R_TSHI + 2 * q);
+                ok &= lo >= -1 && lo < NSQ && hi >= -1 && hi < NSQ;
+            }
+        }
+        const int prop = fld<int16_t>(rec, R_PROP);
+        ok &= prop >= -1 && prop < NACT;
+    }
+    return __all_sync(FULL, ok);
+}
+
+// ---------------------------------------------------------------------------
 // The per-env kernel
 // ---------------------------------------------------------------------------
 
@@ -1240,7 +1294,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
             continue;
         }
         const int64_t e = base + w;
-        const bool live = e < a.n;
+        bool live = e < a.n;
         if (live) {
             reinterpret_cast<uint2*>(rec)[lane] = reinterpret_cast<const uint2*>(a.rec + e * REC)[lane];
             __syncwarp();
@@ -1254,6 +1308,12 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
             zob_wait();
             reset_env(rec, ring2, a, s_zob, e, has(F_RESET_POOL), lane, isf_on);
             dirty = true;
+        }
+        if (kDebugBounds && live && !record_ok(rec, lane, a.rules)) {
+            // the game is skipped: its record and outputs stay as they are
+            if (lane == 0 && a.status) atomicOr(a.status, SB_STATUS_BAD_STATE);
+            live = false;
+            dirty = false;
         }
 
         for (int p = 0; p < np; ++p, ++iter) {
@@ -1368,14 +1428,16 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
             if (has(F_PROPOSE) || has(F_SAMPLE_OUT)) {
                 int ac;
                 float lp;
-                choose<kPol>(Pick{a.seed, a.env_base, a.logits, a.policy}, rays, n, e, pp, lane, ac, lp, scratch,
+                // a game that is over (and was not reset) proposes no move: -1, log-prob 0
+                const int n_pick = has(F_PROPOSE) && rec[R_TERM] ? 0 : n;
+                choose<kPol>(Pick{a.seed, a.env_base, a.logits, a.policy}, rays, n_pick, e, pp, lane, ac, lp, scratch,
                              kPol == SB_POLICY_UNIFORM ? &u_prop : nullptr);
                 if (lane == 0) {
                     if (has(F_PROPOSE)) {
                         fld<int16_t>(rec, R_PROP) = (int16_t)ac;
                         fld<int32_t>(rec, R_PROPPLY) = a.logits ? -1 : (int32_t)pp;
                         rec[R_PROPKIND] = (uint8_t)(kPol >= 0 ? kPol : a.policy);
-                        fld<int16_t>(rec, R_NLEGAL) = (int16_t)n;
+                        fld<int16_t>(rec, R_NLEGAL) = (int16_t)n_pick;
                         fld<float>(rec, R_PROPLP) = lp;
                         if (a.next_action) a.next_action[in] = (int16_t)ac;
                         if (a.next_logprob) a.next_logprob[in] = lp;
@@ -1502,6 +1564,10 @@ __global__ void __launch_bounds__(WARPS * 32) belief_kernel(const uint8_t* root_
             for (int i = lane; i < ISF_TS_BYTES / 8; i += 32) dst[i] = src[i];
         }
         __syncwarp();
+        if (kDebugBounds && !record_ok(rec, lane, a.rules)) {
+            if (lane == 0 && a.status) atomicOr(a.status, SB_STATUS_BAD_STATE);
+            continue;  // the sample is left as it was
+        }
         const int opp = 1 - rec[R_PLAYER];
         unsigned hid[4], mov[4];
 #pragma unroll
@@ -1946,6 +2012,8 @@ int noalloc_staging(int64_t** out) {
 extern "C" {
 
 int sb_abi_version(void) { return SB_ABI_VERSION; }
+
+int sb_debug_bounds(void) { return sb::kDebugBounds ? 1 : 0; }
 
 const char* sb_last_error(void) { return g_err; }
 

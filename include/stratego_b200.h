@@ -88,6 +88,9 @@ typedef struct sb_state {
 
 #define SB_STATUS_BAD_SETUP 1   /* a setup plane or pool entry held a piece code > 12 */
 #define SB_STATUS_WAIT_TIMEOUT 2 /* a kernel gave up waiting (about 1 s) on an in-CTA handshake */
+#define SB_STATUS_BAD_STATE 4   /* debug build only: a game record failed its bounds checks (a piece
+                                   code, a history / chase-ring head, length or entry, a square or
+                                   action index out of range); that game was skipped, untouched */
 
 /* Outputs of one fused step; any pointer may be NULL (not produced). */
 typedef struct sb_step_out {
@@ -100,7 +103,8 @@ typedef struct sb_step_out {
     uint8_t *done;             /* [n] 1 if the transition ended the game */
     int64_t *action_taken;     /* [n] action applied this step (-1 none) */
     float *logprob_taken;      /* [n] log-prob of the applied action when sampled */
-    int16_t *next_action;      /* [n] action proposed for the new state (-1 none) */
+    int16_t *next_action;      /* [n] action proposed for the new state (-1 none: no legal
+                                  move, or the game is over and was not reset) */
     float *next_logprob;       /* [n] its log-prob */
     int64_t *hash;             /* [n] Zobrist hash of the new board */
     int64_t *stats;            /* [5] accumulated over games that ended this step:
@@ -117,6 +121,12 @@ typedef struct sb_policy {
 /* ---- version / errors ------------------------------------------------ */
 int sb_abi_version(void);
 const char *sb_last_error(void);
+/* 1 in the debug build (libstratego_b200_debug.so, compiled with
+ * -DSB_DEBUG_BOUNDS): every kernel that plays or observes a game first checks
+ * its record's indices and skips a bad game with SB_STATUS_BAD_STATE instead
+ * of reading or writing out of range.  0 in the production build, which
+ * trusts records that only its own kernels (or sb_init_state / resets) wrote. */
+int sb_debug_bounds(void);
 
 /* ---- construction ------------------------------------------------------
  * Initial state of a fresh buffer: empty board, Red to move, outcome ongoing,
@@ -244,7 +254,8 @@ typedef struct sb_traj {
     int32_t info_layout;
     uint8_t *mask_u8;          /* [T,n,100,100] legal mask of the slot's state */
     uint8_t *mask_bits;        /* [T,n,1250] bit-packed legal mask of the slot's state */
-    int16_t *action;           /* [T,n] action sampled at the slot's state */
+    int16_t *action;           /* [T,n] action sampled at the slot's state (-1 when that
+                                  state is a finished game, which no move leaves) */
     float *logprob;            /* [T,n] its log-prob under the policy */
     float *reward;             /* [T,n] player-0 reward of the slot's transition */
     uint8_t *done;             /* [T,n] the slot's transition ended the game */
