@@ -229,11 +229,14 @@ class BatchedRolloutEngine:
             return out.infostate if out.infostate.dtype == self.obs_dtype else out.infostate.to(self.obs_dtype)
         return states.compute_infostate_tensor(self.obs_dtype)
 
-    def rollout(self, states: StrategoRolloutBuffer, depth: int = 40) -> torch.Tensor:
+    def rollout(self, states: StrategoRolloutBuffer, depth: int = 40,
+                trace: list[torch.Tensor] | None = None) -> torch.Tensor:
         """Advance every game of ``states`` in place by up to ``depth`` plies
         (a game that ends stops), then return ``P(win) - P(loss)`` of the
         network's value head at each final position, for the side to move
-        there (rollouts.py:46-104).  float32 [N] on the buffer's device."""
+        there (rollouts.py:46-104).  float32 [N] on the buffer's device.
+        ``trace``, when given, receives each ply's applied actions ([N] int64,
+        -1 for a game that had ended)."""
         n = states.n_games
         info = self._info(states)
         for _ in range(int(depth)):
@@ -241,6 +244,8 @@ class BatchedRolloutEngine:
                 break
             _, policy = _net_out(self.move_net, info, None)
             out = states.step(None, policy="gumbel", logits=_logits(policy, n), auto_reset=False)
+            if trace is not None:
+                trace.append(out.action.clone())
             info = self._info(states, out)
         value, _ = _net_out(self.move_net, info, None)
         if value is None:
