@@ -5,11 +5,12 @@
 // move validation / combat / trackers / terminal check, auto-reset from the
 // setup pool, and the observation outputs of the new state (legal mask,
 // 488-channel infostate) in a single pass over the env's 256-byte record
-// staged in shared memory.  Dense output rows are stored straight from
-// registers as whole rows; in the single-ply production step a producer warp
-// per CTA streams the zero rows with bulk asynchronous copies
+// staged in shared memory.  Output rows are stored straight from registers
+// as whole rows; in the single-ply production step a producer warp per CTA
+// streams the move-history planes' zero rows with bulk asynchronous copies
 // (cp.async.bulk.global.shared::cta, the TMA engine, no multicast) while the
-// other warps play, and the one-hots land on top after an mbarrier handshake.
+// other warps play, and the history's +1 / -1 land on top after an mbarrier
+// handshake.
 //
 // Semantics follow the reference simulator csrc/stratego_buffer.cu (cited per
 // function) with the Zobrist hash kept incrementally in the record instead of
@@ -923,36 +924,29 @@ __device__ void write_info_dense(const uint8_t* rec, const KArgs& a, int lane, u
 }
 
 // Sparse planes: 0-11 (one 1 per own piece) and 456-487 (the k-th most recent
-// move's +1 at dst, -1 at src).  Without a producer warp, planes 0-11 are
-// written as whole rows and the history planes as zero rows; after a
-// producer warp streamed all their zero rows (kZerosDone), only the non-zeros
-// are stored.  The history non-zeros follow in both cases.
+// move's +1 at dst, -1 at src).  Planes 0-11 are written as whole rows (one
+// byte compare per type); the history planes as zero rows -- unless a
+// producer warp streamed those already (kHistZeroed) -- and then the history
+// non-zeros on top, from the same warp right away.  Every line is thus
+// written completely within a short window: patching lines written much
+// earlier measured slower once the output stream keeps the L2 full (the
+// earlier lines are no longer in L2 when the patch arrives).
 // DENSE_ALL also zeroes planes 43-455.
-template <typename T, bool kZerosDone>
+template <typename T, bool kHistZeroed>
 __device__ void write_info_sparse(const uint8_t* rec, int lane, uint8_t* g, int hist_off, bool all) {
     using Q = Quad<T>;
     constexpr int PB = InfoGeom<T>::PB;
     if (lane < 25) {
         uint8_t* gl = g + lane * 4 * (int)sizeof(T);
         const SqFeat f = square_features(rec, lane);
-        if (!kZerosDone) {
-            // own pieces (planes 0-11) as whole rows, one byte compare per
-            // type; the move-history planes as zero rows
-            const uint32_t ONE = Q::bits(IV<T>::from(1.0f));
+        const uint32_t ONE = Q::bits(IV<T>::from(1.0f));
 #pragma unroll
-            for (int t = 0; t < 12; ++t)
-                Q::st(gl + t * PB, Q::ones(__vcmpeq4(f.ot, (uint32_t)(t + 1) * 0x01010101u) & 0x01010101u, ONE));
+        for (int t = 0; t < 12; ++t)
+            Q::st(gl + t * PB, Q::ones(__vcmpeq4(f.ot, (uint32_t)(t + 1) * 0x01010101u) & 0x01010101u, ONE));
+        if (!kHistZeroed) {
             const typename Q::V Z = Q::splat(0u);
 #pragma unroll 8
             for (int k = 0; k < 32; ++k) Q::st(gl + hist_off + k * PB, Z);
-        } else {
-            // own one-hots on the producer's zero rows
-            T* g1 = reinterpret_cast<T*>(g);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const uint32_t pc = (f.ot >> (8 * j)) & 0xFF;
-                if (pc) g1[(pc - 1) * NSQ + 4 * lane + j] = IV<T>::from(1.0f);
-            }
         }
     }
     __syncwarp();
@@ -969,31 +963,12 @@ __device__ void write_info_sparse(const uint8_t* rec, int lane, uint8_t* g, int 
     }
 }
 
-// Zero rows of one env's outputs streamed by the TMA engine (bulk copies from
-// the CTA's zero buffer, no multicast): the whole u8 mask row, infostate
-// planes 0-11 and 456-487.  Issued by the producer lane.
+// The zero rows of one env's history planes (456-487), streamed by the TMA
+// engine as one bulk copy from the CTA's zero buffer (no multicast); issued
+// by the producer lane.
 template <typename T>
-__device__ void bulk_zero_rows(const uint8_t* zb, uint8_t* gmask, uint8_t* ginfo, int hist_off) {
-    constexpr int PB = InfoGeom<T>::PB;
-    if (gmask) bulk_s2g(gmask, zb, NACT);
-    if (ginfo) {
-        bulk_s2g(ginfo, zb, 12 * PB);
-        bulk_s2g(ginfo + hist_off, zb, 32 * PB);
-    }
-}
-
-// u8 legal-mask ones on top of a zeroed row (MODE_STEP_PROD).
-__device__ void mask_scatter(const uint16_t* rays, int lane, uint8_t* m) {
-    // rolled loops: every lane walks a different number of moves, and the
-    // unrolled form would multiply the code the warps fetch
-#pragma unroll 1
-    for (int sq = lane; sq < NSQ; sq += 32) {
-        const uint32_t r = rays[sq];
-        const int n = (r & 15) + ((r >> 4) & 15) + ((r >> 8) & 15) + (r >> 12);
-        uint8_t* row = m + sq * 100;
-#pragma unroll 1
-        for (int j = 0; j < n; ++j) row[decode_ray(sq, r, j)] = 1;
-    }
+__device__ void bulk_zero_history(const uint8_t* zb, uint8_t* ginfo, int hist_off) {
+    bulk_s2g(ginfo + hist_off, zb, 32 * InfoGeom<T>::PB);
 }
 
 // Legal mask (csrc/stratego_buffer.cu:448-507) of the side to move, built
@@ -1220,6 +1195,18 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
         mbar_fence_init();
     }
     __syncthreads();
+    if (producer) {
+        for (int i = lane; i < ZERO_BYTES / 16; i += 32) st16(zb + i * 16, make_uint4(0, 0, 0, 0));
+        fence_async_smem();
+        __syncwarp();
+    }
+    // Programmatic dependent launch (host side: launch_mode).  The next
+    // launch on the stream may start its own prologue now, on SMs this launch
+    // leaves; this launch waits here until the launch before it has completed
+    // and its writes are visible, before touching global memory.  Both are
+    // no-ops for a launch made without the attribute.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     // The Zobrist table lives in shared memory, so the game logic never waits
     // on HBM for it while the outputs stream out.  One bulk copy brings it in
     // while the warps load their records; a warp waits for it only before
@@ -1235,11 +1222,6 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
             zob_ready = true;
         }
     };
-    if (producer) {
-        for (int i = lane; i < ZERO_BYTES / 16; i += 32) st16(zb + i * 16, make_uint4(0, 0, 0, 0));
-        fence_async_smem();
-        __syncwarp();
-    }
     uint8_t* rec = ws;
     uint16_t* rays = reinterpret_cast<uint16_t*>(ws + SM_RAYS);
     uint16_t* scratch = reinterpret_cast<uint16_t*>(ws + SM_SCRATCH);
@@ -1250,7 +1232,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
     const int hist_off = (compact ? 44 : 456) * PB;
     // MODE_STEP_PROD is single-ply: one batch of envs per iteration
     const int np = (kStep && !kProd && a.n_plies > 1) ? a.n_plies : 1;
-    const bool zeros = kProd && (has(F_INFO) || has(F_MASK_U8));
+    const bool zeros = kProd && has(F_INFO);  // the producer streams the history planes' zero rows
     const int64_t stride = (int64_t)gridDim.x * ENVW;
     const int64_t first = (int64_t)blockIdx.x * ENVW;
     int64_t iter = 0;
@@ -1278,9 +1260,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                     const int64_t s_next = has(F_APPLY) ? (a.slot0 + 1) % a.n_slots : a.slot0 % a.n_slots;
                     for (int j = 0; j < ENVW && base + j < a.n; ++j) {
                         const int64_t in = s_next * a.n + base + j;
-                        bulk_zero_rows<T>(zb, has(F_MASK_U8) ? a.mask_u8 + in * NACT : nullptr,
-                                          has(F_INFO) ? reinterpret_cast<uint8_t*>(a.info) + in * info_env : nullptr,
-                                          hist_off);
+                        bulk_zero_history<T>(zb, reinterpret_cast<uint8_t*>(a.info) + in * info_env, hist_off);
                     }
                     bulk_commit();
                     bulk_wait_all();
@@ -1468,8 +1448,8 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
             __syncwarp();
             // outputs of the new state.  Dense rows need no zero pass.  In
             // MODE_STEP_PROD the odd warps write them last, so that their
-            // bandwidth-bound stream overlaps the even warps' scattered stores
-            // (request-bound) and the other way round.
+            // stream overlaps the even warps' sparse and mask rows and the
+            // other way round.
             if (has(F_INFO) && !(zeros && (w & 1))) write_info_dense<T>(rec, a, lane, ginfo);
           }
             if (zeros) {
@@ -1481,20 +1461,11 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
             }
           if (live) {
             const bool all = a.info_layout == SB_LAYOUT_DENSE_ALL;
-            if (kProd) {
-                if (has(F_INFO)) write_info_sparse<T, true>(rec, lane, ginfo, hist_off, all);
-                if (has(F_MASK_U8)) mask_scatter(rays, lane, a.mask_u8 + in * NACT);
-                if (has(F_MASK_BITS)) {
-                    build_mask_bits(rays, lane, wbits);
-                    write_mask_bits(wbits, lane, a.mask_bits + in * SB_MASK_BITS_BYTES);
-                }
-            } else {
-                if (has(F_INFO)) write_info_sparse<T, false>(rec, lane, ginfo, hist_off, all);
-                if (has(F_MASK_U8) || has(F_MASK_BITS)) {
-                    build_mask_bits(rays, lane, wbits);
-                    if (has(F_MASK_U8)) write_mask_u8(wbits, lane, a.mask_u8 + in * NACT);
-                    if (has(F_MASK_BITS)) write_mask_bits(wbits, lane, a.mask_bits + in * SB_MASK_BITS_BYTES);
-                }
+            if (has(F_INFO)) write_info_sparse<T, kProd>(rec, lane, ginfo, hist_off, all);
+            if (has(F_MASK_U8) || has(F_MASK_BITS)) {
+                build_mask_bits(rays, lane, wbits);
+                if (has(F_MASK_U8)) write_mask_u8(wbits, lane, a.mask_u8 + in * NACT);
+                if (has(F_MASK_BITS)) write_mask_bits(wbits, lane, a.mask_bits + in * SB_MASK_BITS_BYTES);
             }
             if (zeros && (w & 1) && has(F_INFO)) write_info_dense<T>(rec, a, lane, ginfo);
             __syncwarp();
@@ -1549,6 +1520,10 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
 __global__ void __launch_bounds__(WARPS * 32) belief_kernel(const uint8_t* root_rec, int64_t n_roots,
                                                            const int64_t* root_of, KArgs a, const uint8_t* root_isf) {
     __shared__ __align__(16) uint8_t srec[WARPS][REC];
+    // lane 0's Fisher-Yates lists: moved / unmoved hidden squares, the
+    // identities (movable ones first), and the movable / immobile identities
+    // as found; in shared memory, not in local memory
+    __shared__ uint8_t s_fy[WARPS][5][40];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     uint8_t* rec = srec[w];
     const int64_t nwarps = (int64_t)gridDim.x * WARPS;
@@ -1580,9 +1555,8 @@ __global__ void __launch_bounds__(WARPS * 32) belief_kernel(const uint8_t* root_
         }
         if (lane == 0) {
             if (bad && a.status) atomicOr(a.status, SB_STATUS_BAD_SETUP);
-            uint8_t msq[40], usq[40], pcs[40];
+            uint8_t *msq = s_fy[w][0], *usq = s_fy[w][1], *pcs = s_fy[w][2], *movp = s_fy[w][3], *immp = s_fy[w][4];
             int nm = 0, nu = 0, nmov = 0, nimm = 0;
-            uint8_t movp[40], immp[40];
             for (int k = 0; k < 4; ++k) {
                 unsigned hb = hid[k];
                 while (hb) {
@@ -1603,19 +1577,16 @@ __global__ void __launch_bounds__(WARPS * 32) belief_kernel(const uint8_t* root_
             for (int i = 0; i < nmov; ++i) pcs[np_++] = movp[i];
             for (int i = 0; i < nimm; ++i) pcs[np_++] = immp[i];
             const int64_t ge = a.env_base + e;
-            uint32_t words[4];
+            uint4 words = make_uint4(0, 0, 0, 0);
             int used = 4, blk = 0;
             auto draw = [&](uint32_t bound) -> int {
                 if (used == 4) {
-                    const uint4 q = philox((uint32_t)ge, (uint32_t)blk++, (uint32_t)((uint64_t)ge >> 32), TAG_BELIEF,
-                                           a.seed);
-                    words[0] = q.x;
-                    words[1] = q.y;
-                    words[2] = q.z;
-                    words[3] = q.w;
+                    words = philox((uint32_t)ge, (uint32_t)blk++, (uint32_t)((uint64_t)ge >> 32), TAG_BELIEF, a.seed);
                     used = 0;
                 }
-                return (int)mulshift(words[used++], bound);
+                const uint32_t wd = used == 0 ? words.x : (used == 1 ? words.y : (used == 2 ? words.z : words.w));
+                ++used;
+                return (int)mulshift(wd, bound);
             };
             // 1) moved squares draw from the movable identities (partial Fisher-Yates)
             const int take = nm < nmov ? nm : nmov;
@@ -1934,8 +1905,20 @@ int launch_mode(sb::KArgs& k, cudaStream_t st) {
     int64_t blocks = (k.n + envw - 1) / envw;
     const int64_t cap = (int64_t)sms * nb;
     if (blocks > cap) blocks = cap;
-    sb::env_kernel<T, MODE><<<(unsigned)blocks, sb::WARPS * 32, smem, st>>>(k);
-    e = cudaGetLastError();
+    // programmatic dependent launch: this grid's CTAs may become resident
+    // while the previous launch on the stream drains; the kernel waits
+    // (griddepcontrol.wait) before it touches global memory
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)blocks);
+    cfg.blockDim = dim3(sb::WARPS * 32);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, sb::env_kernel<T, MODE>, k);
     if (e != cudaSuccess) return cuda_fail(e, "env_kernel launch");
     return SB_OK;
 }
