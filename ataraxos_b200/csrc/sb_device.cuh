@@ -110,6 +110,30 @@ __device__ __forceinline__ uint4 philox(uint32_t c0, uint32_t c1, uint32_t c2, u
     return make_uint4(c0, c1, c2, c3);
 }
 
+// The same generator with its ten round keys precomputed (rk[2r], rk[2r+1] =
+// the key halves after r bumps): kernels read them from their parameter block,
+// so each round's key enters the XOR as an operand instead of being bumped
+// with two additions.
+__host__ __device__ __forceinline__ void philox_round_keys(uint64_t seed, uint32_t rk[20]) {
+    uint32_t k0 = (uint32_t)seed, k1 = (uint32_t)(seed >> 32);
+    for (int r = 0; r < 10; ++r) {
+        rk[2 * r] = k0;
+        rk[2 * r + 1] = k1;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+}
+__device__ __forceinline__ uint4 philox_rk(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, const uint32_t* rk) {
+#pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        uint32_t hi0 = __umulhi(0xD2511F53u, c0), lo0 = 0xD2511F53u * c0;
+        uint32_t hi1 = __umulhi(0xCD9E8D57u, c2), lo1 = 0xCD9E8D57u * c2;
+        uint32_t n0 = hi1 ^ c1 ^ rk[2 * r], n2 = hi0 ^ c3 ^ rk[2 * r + 1];
+        c0 = n0; c1 = lo1; c2 = n2; c3 = lo0;
+    }
+    return make_uint4(c0, c1, c2, c3);
+}
+
 __device__ __forceinline__ uint32_t mulshift(uint32_t u, uint32_t n) {
     return (uint32_t)(((uint64_t)u * (uint64_t)n) >> 32);
 }

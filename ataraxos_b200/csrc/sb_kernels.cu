@@ -53,6 +53,7 @@ struct KArgs {
     int64_t n;
     int64_t env_base;
     uint64_t seed;
+    uint32_t rk[20];  // Philox round keys of `seed` (philox_round_keys)
     int32_t no_attack_limit, max_len, ts_limit, policy;
     int32_t* status;
     const float* logits;
@@ -301,7 +302,7 @@ __device__ int kth_action(int kth, const uint16_t* rays, int lane) {
 // acts: the warp's shared-memory scratch (at least 200 bytes).
 // u_pre: the uniform policy's Philox word when the caller drew it already.
 struct Pick {
-    uint64_t seed;
+    const uint32_t* rk;   // Philox round keys (in the kernel's parameter block)
     int64_t env_base;
     const float* logits;  // [n,10000] or nullptr (virtual N(0,1) logits)
     int policy;
@@ -319,7 +320,7 @@ __device__ void choose(const Pick& a, const uint16_t* rays, int n, int64_t e, in
     const int pol = POL >= 0 ? POL : a.policy;
     if (pol == SB_POLICY_UNIFORM) {
         const uint32_t u =
-            u_pre ? *u_pre : philox((uint32_t)ge, (uint32_t)ply, (uint32_t)((uint64_t)ply >> 32), TAG_ACTION, a.seed).x;
+            u_pre ? *u_pre : philox_rk((uint32_t)ge, (uint32_t)ply, (uint32_t)((uint64_t)ply >> 32), TAG_ACTION, a.rk).x;
         act = kth_action((int)mulshift(u, (uint32_t)n), rays, lane);
         lp = -xln((float)n);
         return;
@@ -371,7 +372,7 @@ __device__ void choose(const Pick& a, const uint16_t* rays, int n, int64_t e, in
                 mx = fmaxf(mx, lg[ac]);
                 continue;
             }
-            const uint4 w = philox((uint32_t)ge, (uint32_t)ply, (uint32_t)ac, TAG_LOGIT, a.seed);
+            const uint4 w = philox_rk((uint32_t)ge, (uint32_t)ply, (uint32_t)ac, TAG_LOGIT, a.rk);
             const float z = lg ? lg[ac]
                                : __fmul_rn(__fsqrt_rn(__fmul_rn(-2.0f, xln(unit_open(w.x)))), xcos2pi(unit_open(w.y)));
             const float q = xexp(__fsub_rn(z, shift));
@@ -416,10 +417,10 @@ __device__ void choose(const Pick& a, const uint16_t* rays, int n, int64_t e, in
 // The policy's inputs come as scalars (not the kernel's argument block,
 // whose address would need a local-memory copy).
 template <int POL>
-__device__ __noinline__ void choose_cold(uint64_t seed, int64_t env_base, const float* logits, int policy,
+__device__ __noinline__ void choose_cold(const uint32_t* rk, int64_t env_base, const float* logits, int policy,
                                          const uint16_t* rays, int n, int64_t e, int64_t ply, int lane, int& act,
                                          float& lp, uint16_t* scratch) {
-    choose<POL>(Pick{seed, env_base, logits, policy}, rays, n, e, ply, lane, act, lp, scratch);
+    choose<POL>(Pick{rk, env_base, logits, policy}, rays, n, e, ply, lane, act, lp, scratch);
 }
 
 // ---------------------------------------------------------------------------
@@ -436,7 +437,7 @@ __device__ void reset_env(uint8_t* rec, int64_t* ring2, const KArgs& a, const in
     const int32_t ep = fld<int32_t>(rec, R_EPISODE);
     if (from_pool) {
         const int64_t ge = a.env_base + e;
-        const uint4 w = philox((uint32_t)ge, (uint32_t)ep, (uint32_t)((uint64_t)ge >> 32), TAG_RESET, a.seed);
+        const uint4 w = philox_rk((uint32_t)ge, (uint32_t)ep, (uint32_t)((uint64_t)ge >> 32), TAG_RESET, a.rk);
         const uint64_t ri = ((uint64_t)w.x * (uint64_t)a.pool_size) >> 32;
         const uint64_t bi = ((uint64_t)w.y * (uint64_t)a.pool_size) >> 32;
         red = a.pool + ri * 40;
@@ -1161,7 +1162,7 @@ __device__ int serve_wait(const KArgs& a, int64_t t) {
 }
 
 template <typename T, int MODE>
-__global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
+__global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const __grid_constant__ KArgs a) {
     constexpr int M = MODE & ~(MODE_ISF | MODE_SERVE);
     constexpr bool kServe = (MODE & MODE_SERVE) != 0;
     constexpr bool kStep = M != MODE_GENERIC;
@@ -1311,7 +1312,8 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
             const int64_t pp = has(F_PROPOSE) ? (has(F_APPLY) ? ply + 1 : ply) : ply_base;
             uint32_t u_prop = 0;
             if (kPol == SB_POLICY_UNIFORM)
-                u_prop = philox((uint32_t)(a.env_base + e), (uint32_t)pp, (uint32_t)((uint64_t)pp >> 32), TAG_ACTION, a.seed).x;
+                u_prop = philox_rk((uint32_t)(a.env_base + e), (uint32_t)pp, (uint32_t)((uint64_t)pp >> 32), TAG_ACTION,
+                                   a.rk).x;
           if (live) {
             struct {
                 bool valid = false, term = false, ended = false;
@@ -1340,7 +1342,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                             n_legal = enumerate(rec, pm, rays, lane);
                             if (!a.actions) {
                                 int ac;
-                                choose_cold<kPol>(a.seed, a.env_base, a.logits, a.policy, rays, n_legal, e, ply, lane, ac,
+                                choose_cold<kPol>(a.rk, a.env_base, a.logits, a.policy, rays, n_legal, e, ply, lane, ac,
                                                   lp, scratch);
                                 act = ac;
                             }
@@ -1410,7 +1412,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
                 float lp;
                 // a game that is over (and was not reset) proposes no move: -1, log-prob 0
                 const int n_pick = has(F_PROPOSE) && rec[R_TERM] ? 0 : n;
-                choose<kPol>(Pick{a.seed, a.env_base, a.logits, a.policy}, rays, n_pick, e, pp, lane, ac, lp, scratch,
+                choose<kPol>(Pick{a.rk, a.env_base, a.logits, a.policy}, rays, n_pick, e, pp, lane, ac, lp, scratch,
                              kPol == SB_POLICY_UNIFORM ? &u_prop : nullptr);
                 if (lane == 0) {
                     if (has(F_PROPOSE)) {
@@ -1518,7 +1520,8 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const KArgs a) {
 // its chase rings start empty (their hashes described the true identities)
 // and its Zobrist hash is recomputed.
 __global__ void __launch_bounds__(WARPS * 32) belief_kernel(const uint8_t* root_rec, int64_t n_roots,
-                                                           const int64_t* root_of, KArgs a, const uint8_t* root_isf) {
+                                                           const int64_t* root_of, const __grid_constant__ KArgs a,
+                                                           const uint8_t* root_isf) {
     __shared__ __align__(16) uint8_t srec[WARPS][REC];
     // lane 0's Fisher-Yates lists: moved / unmoved hidden squares, the
     // identities (movable ones first), and the movable / immobile identities
@@ -1581,7 +1584,7 @@ __global__ void __launch_bounds__(WARPS * 32) belief_kernel(const uint8_t* root_
             int used = 4, blk = 0;
             auto draw = [&](uint32_t bound) -> int {
                 if (used == 4) {
-                    words = philox((uint32_t)ge, (uint32_t)blk++, (uint32_t)((uint64_t)ge >> 32), TAG_BELIEF, a.seed);
+                    words = philox_rk((uint32_t)ge, (uint32_t)blk++, (uint32_t)((uint64_t)ge >> 32), TAG_BELIEF, a.rk);
                     used = 0;
                 }
                 const uint32_t wd = used == 0 ? words.x : (used == 1 ? words.y : (used == 2 ? words.z : words.w));
@@ -1807,6 +1810,7 @@ sb::KArgs base_args(const sb_state* s) {
     k.n = s->n;
     k.env_base = s->env_base;
     k.seed = s->seed;
+    sb::philox_round_keys(s->seed, k.rk);
     k.no_attack_limit = s->no_attack_limit;
     k.max_len = s->max_game_length;
     k.ts_limit = s->two_square_limit;
