@@ -83,10 +83,12 @@ struct KArgs {
     // Ply p of a launch reads its transition outputs (reward, done, taken
     // action) at slot (slot0 + p) % n_slots and writes the observation of the
     // new state (mask, infostate, proposal, hash) at slot (slot0 + p + 1) %
-    // n_slots; every output array is laid out [n_slots, n, ...].
+    // n_slots; every output array is laid out [n_slots, n, ...].  The host
+    // passes slot0 already reduced (0 <= slot0 < n_slots < 2^31), so the
+    // kernel walks the ring with counters instead of dividing.
     int32_t n_plies;
-    int64_t n_slots;
-    int64_t slot0;
+    int32_t n_slots;
+    int32_t slot0;
     int32_t rules;  // SB_RULES_*
     uint8_t* isf;   // [n, ISF_TS_BYTES] under SB_RULES_ISF
     // step server (MODE_SERVE): control block in mapped page-locked host
@@ -1258,7 +1260,7 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const __grid_constan
                 if (iter > 0 && !mbar_wait(&s_bar[2], (uint32_t)((iter - 1) & 1)) && lane == 0 && a.status)
                     atomicOr(a.status, SB_STATUS_WAIT_TIMEOUT);
                 if (lane == 0) {
-                    const int64_t s_next = has(F_APPLY) ? (a.slot0 + 1) % a.n_slots : a.slot0 % a.n_slots;
+                    const int64_t s_next = has(F_APPLY) ? (a.slot0 + 1 == a.n_slots ? 0 : a.slot0 + 1) : a.slot0;
                     for (int j = 0; j < ENVW && base + j < a.n; ++j) {
                         const int64_t in = s_next * a.n + base + j;
                         bulk_zero_history<T>(zb, reinterpret_cast<uint8_t*>(a.info) + in * info_env, hist_off);
@@ -1297,15 +1299,17 @@ __global__ void __launch_bounds__(WARPS * 32, 4) env_kernel(const __grid_constan
             dirty = false;
         }
 
-        for (int p = 0; p < np; ++p, ++iter) {
+        // ring slots of the ply's transition (s_cur) and of its new state (s_next)
+        int32_t s_cur = a.slot0, s_nx = a.slot0;
+        for (int p = 0; p < np; ++p, ++iter, s_cur = s_nx) {
             // outside MODE_STEP_PROD the CTA's warps start each ply together:
             // they then run the same code and write neighbouring envs' rows
             // at about the same time (measured faster than letting them drift)
             if (!kProd) __syncthreads();
             const int64_t ply = ply_base + p;
-            const int64_t s_cur = (a.slot0 + p) % a.n_slots;
-            const int64_t s_next = has(F_APPLY) ? (a.slot0 + p + 1) % a.n_slots : a.slot0 % a.n_slots;
-            const int64_t ic = s_cur * a.n + e, in = s_next * a.n + e;
+            s_nx = has(F_APPLY) ? (s_cur + 1 == a.n_slots ? 0 : s_cur + 1) : a.slot0;
+            const int32_t s_next = s_nx;
+            const int64_t ic = (int64_t)s_cur * a.n + e, in = (int64_t)s_next * a.n + e;
             uint8_t* ginfo = has(F_INFO) ? reinterpret_cast<uint8_t*>(a.info) + in * info_env : nullptr;
             // the uniform proposal's random word depends only on (seed, env,
             // ply): drawn first, off the game logic's critical path
@@ -2315,15 +2319,16 @@ int sb_rollout(const sb_state* s, int64_t ply, const sb_policy* policy, int auto
     if ((rc = check_policy(policy)) != SB_OK) return rc;
     if (!traj) return fail(SB_E_ARG, "traj is NULL");
     if (n_plies < 0) return fail(SB_E_ARG, "n_plies < 0");
-    if (traj->n_slots < 1 || traj->slot0 < 0) return fail(SB_E_ARG, "bad trajectory ring (n_slots < 1 or slot0 < 0)");
+    if (traj->n_slots < 1 || traj->n_slots > 0x7FFFFFFFll || traj->slot0 < 0)
+        return fail(SB_E_ARG, "bad trajectory ring (n_slots outside 1..2^31-1, or slot0 < 0)");
     if (policy && policy->logits && n_plies > 1) return fail(SB_E_ARG, "logits in memory cover one ply only");
     if (auto_reset && n_plies > 0 && !s->setup_pool) return fail(SB_E_NOPOOL, "auto_reset needs a setup pool");
     sb::KArgs k = base_args(s);
     k.flags = sb::F_APPLY | sb::F_STEP | sb::F_PROPOSE | (auto_reset ? sb::F_AUTO_RESET : 0);
     k.ply = ply;
     k.n_plies = n_plies;
-    k.n_slots = traj->n_slots;
-    k.slot0 = traj->slot0;
+    k.n_slots = (int32_t)traj->n_slots;
+    k.slot0 = (int32_t)(traj->slot0 % traj->n_slots);
     if (policy) {
         k.policy = policy->kind;
         k.logits = policy->logits;
