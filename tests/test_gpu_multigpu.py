@@ -1,7 +1,7 @@
-"""NCCL ranks on two GPUs of one box: env shards keyed by the global env index
-reproduce a one-GPU run game for game, and the episode-statistics all-gather
-sums to the one-GPU counters.  Skipped on a one-GPU box (the same logic runs on
-gloo CPU ranks in ``test_multirank.py``)."""
+"""NCCL ranks on 2, 4 and 8 GPUs of one box: env shards keyed by the global
+env index reproduce a one-GPU run game for game, and the episode-statistics
+all-gather sums to the one-GPU counters.  Each case is skipped on a box with
+fewer GPUs (the same logic runs on gloo CPU ranks in ``test_multirank.py``)."""
 
 from __future__ import annotations
 
@@ -24,12 +24,18 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_nccl_shards_equal_one_gpu_run():
+def _gpus() -> int:
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_nccl_shards_equal_one_gpu_run(world):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            str(HERE / "_nccl_shard_worker.py")]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    assert "multigpu shard check world=2: ok" in r.stdout
+    assert f"multigpu shard check world={world}: ok" in r.stdout
