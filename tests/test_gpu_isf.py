@@ -75,6 +75,42 @@ def test_isf_golden_games(golden, kind, path):
     assert (export_np(b)["invalid_count"] == 0).all()
 
 
+@pytest.mark.parametrize("path", ["step", "apply"])
+def test_isf_long_chases_match_oracle(path):
+    """Chases around loops of 60-84 squares (tests/golden/isf_long_chase.npz):
+    the kernel's sticky chasing flag rises where the oracle's does -- the
+    reference's verdict while the loop is at most 64 squares long (the chase
+    memory), never for the longer loops -- and the full state, chase rings
+    included, equals the oracle's."""
+    from ataraxos_b200 import StrategoRolloutBuffer
+
+    with np.load(Path(__file__).resolve().parent / "golden" / "isf_long_chase.npz") as f:
+        g = {k: f[k] for k in f.files}
+    n, plies = g["actions"].shape
+    nal = int(g["no_attack_limit"][0])
+    b = StrategoRolloutBuffer(n, 0, no_attack_limit=nal, rules="isf")
+    o = oracle.OracleState(n, no_attack_limit=nal, rules=oracle.RULES_ISF)
+    red, blue = _planes(g["owner"], g["piece"])
+    b.reset_all(torch.from_numpy(red), torch.from_numpy(blue))
+    o.reset_planes(red, blue, force_all=True)
+    seen = np.zeros(n, bool)
+    short = g["cycle_len"] <= 64
+    for t in range(plies):
+        a = g["actions"][:, t].astype(np.int64)
+        if path == "step":
+            b.step(torch.from_numpy(a), auto_reset=False)
+        else:
+            b.apply_actions(torch.from_numpy(a))
+        o.apply(a)
+        seen |= short & (g["ev_chasing"][:, t] > 0)
+        st = export_np(b)
+        np.testing.assert_array_equal(st["chasing_violation"].astype(bool), seen, err_msg=f"ply {t}")
+        if t % 20 == 0:
+            assert_state_equal(st, o.export(), f"ply {t}")
+    assert seen[short].all() and not seen[~short].any()
+    assert_state_equal(export_np(b), o.export(), "end")
+
+
 @pytest.mark.parametrize("policy", ["uniform", "gumbel"])
 def test_isf_random_games_match_oracle(policy):
     from ataraxos_b200 import StrategoRolloutBuffer

@@ -122,3 +122,38 @@ def test_isf_chase_needs_an_evasion():
     isf.reset_planes(*_board(pieces), force_all=True)
     ev = _play(isf, moves)
     assert int(isf.a["chasing_violation"][0]) == 0 and not any(e & 2 for e in ev)
+
+
+LONG_CHASE = Path(__file__).resolve().parent / "golden" / "isf_long_chase.npz"
+
+
+def test_isf_chase_memory_bound_against_reference():
+    """The one place the ISF chasing rule departs from the reference: a chase
+    remembers its last 64 positions (the reference's set, chasing.py:54-109,
+    is unbounded).  ``isf_long_chase.npz`` (tests/golden/make_golden_isf_chase.py)
+    holds chases around loops of L squares judged by the reference's own
+    tracker, which flags the chaser's return to the chase's first position
+    (ply 2L + 2) and every chasing move after it.  The oracle agrees move for
+    move while L <= 64 and flags nothing once L > 64; two-square verdicts
+    agree everywhere."""
+    with np.load(LONG_CHASE) as f:
+        g = {k: f[k] for k in f.files}
+    n, plies = g["actions"].shape
+    o = oracle.OracleState(n, no_attack_limit=int(g["no_attack_limit"][0]), rules=oracle.RULES_ISF)
+    o.reset_planes(*_planes(g["owner"], g["piece"]), force_all=True)
+    ev = np.zeros((n, plies), np.uint8)
+    for t in range(plies):
+        o.apply(g["actions"][:, t].astype(np.int64))
+        ev[:, t] = o.isf_event
+    assert (o.a["invalid_count"] == 0).all() and (o.a["terminated"] == 0).all()
+    np.testing.assert_array_equal(ev & 1, g["ev_two_square"])
+    for i, L in enumerate(g["cycle_len"]):
+        ref = g["ev_chasing"][i]
+        first = 2 * int(L) + 2
+        # the reference: every Red (chaser) move from ply 2L + 2 on, nothing before
+        assert not ref[:first].any() and ref[first::2].all() and not ref[first + 1::2].any()
+        if L <= 64:
+            np.testing.assert_array_equal((ev[i] >> 1) & 1, ref, err_msg=f"loop {L}")
+        else:
+            assert not ((ev[i] >> 1) & 1).any(), f"loop {L}"
+    assert sorted(g["cycle_len"].tolist()) == [60, 62, 64, 66, 84]
