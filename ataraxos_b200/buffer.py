@@ -603,14 +603,15 @@ class StrategoRolloutBuffer:
         observe: bool = True,
         sync: bool = True,
         mapped: bool = True,
+        stream: torch.cuda.Stream | None = None,
     ) -> HostStepOutput:
         """``step`` for a host-side caller, in one native call: the (N,) int64
         CPU ``actions`` (None: sample on the device) go host->device, the fused
         ply runs, and reward / done / next_action come back into pinned host
         memory with one copy.  The returned host tensors (and ``.device``, the
         step's device outputs) are overwritten by the next call; with
-        ``sync=False`` they are valid once the current stream has reached this
-        call's end.
+        ``sync=False`` they are valid once the stream (``stream``, else the
+        current stream) has reached this call's end.
 
         ``mapped=True`` moves the data without copy-engine transfers: the
         kernel reads the actions from page-locked host memory and writes
@@ -644,10 +645,11 @@ class StrategoRolloutBuffer:
         if torch.cuda.current_device() != dev:
             with torch.cuda.device(self.device):
                 rc = h["fn"](h["st"], h["bio"][mode], self._ply, pol, 1 if auto_reset else 0,
-                             h["out"][mode][bool(observe)], _raw_stream(dev))
+                             h["out"][mode][bool(observe)],
+                             _raw_stream(dev) if stream is None else stream.cuda_stream)
         else:
             rc = h["fn"](h["st"], h["bio"][mode], self._ply, pol, 1 if auto_reset else 0,
-                         h["out"][mode][bool(observe)], _raw_stream(dev))
+                         h["out"][mode][bool(observe)], _raw_stream(dev) if stream is None else stream.cuda_stream)
         if rc:
             C.check(rc)
         self._ply += 1

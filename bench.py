@@ -9,28 +9,40 @@ Default workload = benchmark config 2: 4096 envs per GPU, seeded random setups
 (pool of 65536), uniform random legal actions, auto-reset, bf16 infostate
 [B,488,10,10] (channels 43-455 are zero planes written once at allocation;
 every ply rewrites the 75 live channels), uint8 mask [B,100,100].  One step =
-one ply over all envs = one launch of the fused step kernel.  Synthetic data:
-there is no dataset; setups and actions come from Philox.
+one ply over all envs.  The GPU's envs form ``--groups`` groups (default 3 for
+config 2, 2 for config 3): contiguous global env ranges, each a buffer stepped
+on its own CUDA stream, so one step is one fused-step launch per group and the
+groups' launches run concurrently (one launch's ramp and drain overlap the
+others' work).  Every random stream is keyed by the global env index, so the
+games are the same for any number of groups.  Synthetic data: there is no
+dataset; setups and actions come from Philox.
 
 Timing (config 2, default ``--timing graph``): W untimed warm-up steps, then
 the K timed steps, launched back to back as one CUDA graph (captured after the
-warm-up, each node one fused-step launch with its own ply number) and
-replayed once between two CUDA events on the buffer's stream; barrier +
-synchronize on both sides; max over ranks.  The steps write their outputs
-into 4 output sets in turn (4 x 441 MB, 14x the 126 MB L2), so no step
-writes lines still held in L2 and every step's 104.6 MB of writes reaches
-HBM inside the timed region (the game records, 1 MB, stay in L2 from ply to
-ply, as in any rollout).  ``--timing flush`` is the per-launch form: each
+warm-up; each group's launches a chain on its own stream, each node with its
+own ply number, and two CUDA events recorded in the graph on the stream the
+chains fork from and join, before the fork and after the join), uploaded to
+the device, and replayed once; barrier + synchronize on both sides; max over
+ranks.  Each group writes its outputs into 4 output sets
+in turn (4 x 441 MB in all, 14x the 126 MB L2), so no step writes lines still
+held in L2 and every step's 104.6 MB of writes reaches HBM inside the timed
+region (the game records, 1 MB, stay in L2 from ply to ply, as in any
+rollout).  ``--timing flush`` (one group only) is the per-launch form: each
 step bracketed by its own events, with a 512 MiB write and a 256 MiB read
-between steps (outside the bracketed interval) to flush L2.
+between steps (outside the bracketed interval) to flush L2.  Config 3 (6.7 GB
+written per step) launches the groups' chains from the host between two
+events.
 Multi-GPU (torchrun): each rank owns its own 4096 envs (global env indices
 rank*4096 ...), no collective on the step path (weak scaling); an NCCL
 all-gather of the episode statistics follows the timed region.
 
-e2e: the same steps through the public host API (``step_host``: int64 actions
-from page-locked host memory in, reward / done / next action back into
-page-locked memory, the call returning when they have landed), CUDA events
-around the loop; ``--e2e-api serve`` uses the persistent step server instead.
+e2e: the same games through the public host API with host buffers: int64
+actions from page-locked host memory in, reward / done / next action back into
+page-locked memory every step, the host playing the proposals it received.
+Default ``--e2e-api pipeline``: ``ataraxos_b200.pipeline.StepPipeline`` with
+``--e2e-groups`` groups received and re-sent in turn (each group's ply one
+``sb_step_host`` call); ``step_host``: one synchronous call per step over all
+envs; ``serve``: the persistent step server.  CUDA events around the loop.
 
 ``--impl reference`` times the reference algorithm's CPU implementation on the
 host cores: the C restatement in oracle/ (the reference's own code is Python
@@ -326,28 +338,123 @@ class Ctx:
         return sharding.gather_episode_stats(stats).sum(0).tolist()
 
 
-def timed_graph(ctx: Ctx, launch, first: int, k: int):
-    """launch(first) .. launch(first + k - 1) captured into one CUDA graph,
-    then replayed once between CUDA events (no host work between steps)."""
+class Groups:
+    """The rank's games as ``G`` buffers (contiguous global env ranges), each
+    stepped on its own CUDA stream, so the groups' launches run concurrently:
+    one group's launch ramp and drain overlap the others' work.  Every random
+    stream is keyed by the global env index, so the games play exactly as in
+    one buffer of all of them; one step = one ply of every game = one launch
+    per group."""
+
+    def __init__(self, ctx: Ctx, B: int, env_base: int, G: int, n_sets: int, **buf_kw) -> None:
+        from ataraxos_b200 import StrategoRolloutBuffer
+
+        if not 1 <= G <= B:
+            raise SystemExit(f"--groups must be in 1..{B}")
+        self.parts = []
+        for g in range(G):
+            off, n = sharding.shard_range(B, G, g)
+            s = torch.cuda.Stream(ctx.dev)
+            with torch.cuda.stream(s):
+                b = StrategoRolloutBuffer(n, ctx.local, env_base=env_base + off, **buf_kw)
+                b.reset_all_from_pool()
+                sets = [b._ensure_outputs()] + [b.new_outputs() for _ in range(n_sets - 1)] if n_sets > 1 else [None]
+            self.parts.append((b, s, sets))
+        torch.cuda.synchronize(ctx.dev)
+
+    def step(self, i: int, policy: str) -> None:
+        for b, s, sets in self.parts:
+            with torch.cuda.stream(s):
+                b.step(None, policy=policy, outputs=sets[i % len(sets)])
+
+    def fork(self, main: torch.cuda.Stream) -> None:
+        ev = torch.cuda.Event()
+        ev.record(main)
+        for _, s, _ in self.parts:
+            s.wait_event(ev)
+
+    def join(self, main: torch.cuda.Stream) -> None:
+        for _, s, _ in self.parts:
+            ev = torch.cuda.Event()
+            ev.record(s)
+            main.wait_event(ev)
+
+    def stats(self) -> torch.Tensor:
+        return sum(b.episode_stats().clone() for b, _, _ in self.parts)
+
+    def status(self) -> int:
+        st = 0
+        for b, _, _ in self.parts:
+            st |= int(b.status())
+        return st
+
+
+def _graph_upload(graph: torch.cuda.CUDAGraph, stream: torch.cuda.Stream) -> None:
+    """Upload an instantiated graph to the device before its first launch
+    (cuGraphUpload), so the timed launch does not pay for it."""
+    import ctypes
+
+    cu = ctypes.CDLL("libcuda.so.1")
+    rc = cu.cuGraphUpload(ctypes.c_void_p(graph.raw_cuda_graph_exec()), ctypes.c_void_p(stream.cuda_stream))
+    if rc != 0:
+        raise RuntimeError(f"cuGraphUpload failed: {rc}")
+    stream.synchronize()
+
+
+def timed_graph(ctx: Ctx, groups: Groups, first: int, k: int, policy: str):
+    """Steps first .. first + k - 1 of every group captured into one CUDA graph
+    (each group's launches a chain on its own stream, forked from and joined
+    to one stream, with a CUDA event recorded on that stream before the fork
+    and after the join), uploaded, then replayed once (no host work between
+    steps)."""
+    main = torch.cuda.Stream(ctx.dev)
     g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
+    # the timing events are nodes of the graph (external events): they bracket
+    # the K steps on the device, not the host's launch of the graph
+    e0, e1 = torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True)
+    with torch.cuda.graph(g, stream=main):
+        e0.record(main)
+        groups.fork(main)
         for i in range(first, first + k):
-            launch(i)
+            groups.step(i, policy)
+        groups.join(main)
+        e1.record(main)
     torch.cuda.synchronize(ctx.dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _graph_upload(g, main)
     ctx.barrier()
     torch.cuda.synchronize(ctx.dev)
     torch.cuda.nvtx.range_push("timed")
     with ClockSampler(ctx.dev) as clocks:
-        e0.record(ctx.stream)
-        g.replay()
-        e1.record(ctx.stream)
+        with torch.cuda.stream(main):
+            g.replay()
         torch.cuda.synchronize(ctx.dev)
         ctx.barrier()
     torch.cuda.nvtx.range_pop()
     total_ms = ctx.max_over_ranks(e0.elapsed_time(e1))
     del g
     return total_ms, clocks.summary()
+
+
+def timed_streams(ctx: Ctx, groups: Groups, first: int, k: int, policy: str):
+    """k steps of every group launched from the host (each group's chain on
+    its own stream), forked from and joined to one stream whose CUDA events
+    bracket the whole interval."""
+    main = torch.cuda.Stream(ctx.dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx.barrier()
+    torch.cuda.synchronize(ctx.dev)
+    torch.cuda.nvtx.range_push("timed")
+    with ClockSampler(ctx.dev) as clocks:
+        e0.record(main)
+        groups.fork(main)
+        for i in range(first, first + k):
+            groups.step(i, policy)
+        groups.join(main)
+        e1.record(main)
+        torch.cuda.synchronize(ctx.dev)
+        ctx.barrier()
+    torch.cuda.nvtx.range_pop()
+    return ctx.max_over_ranks(e0.elapsed_time(e1)), clocks.summary()
 
 
 def timed_launches(ctx: Ctx, launch, k: int, flush_mib: int):
@@ -379,118 +486,165 @@ def timed_launches(ctx: Ctx, launch, k: int, flush_mib: int):
     return total_ms, clocks.summary()
 
 
-def e2e_loop(ctx: Ctx, buf, steps: int, policy: str = "uniform", total_envs: int | None = None
+def e2e_loop(ctx: Ctx, B: int, env_base: int, buf_kw: dict, steps: int, policy: str, total: int
              ) -> tuple[float, int, int, str]:
-    """The public host-side API with host buffers: per step the actions
-    (int64[B], page-locked host memory) cross to the device, the fused step
-    runs, and reward, done and the next proposed actions cross back into
-    page-locked host memory; the host takes the proposals as its next actions.
-    By default (``--e2e-api step_host``) every step is one ``step_host`` call
-    (the kernel reads / writes the page-locked memory in place, CUDA events
-    around the loop).  ``--e2e-api serve`` runs uniform steps through the
-    persistent step server instead (``StrategoRolloutBuffer.serve``: no launch
-    or stream synchronisation per step, CUDA events around the server
-    kernel's whole life).  Returns (updates/s, h2d, d2h bytes, api)."""
+    """The public host-side API with host buffers, on the same games as the
+    device-timed steps (same global env indices, seed and pool): per step every
+    game's int64 action crosses from page-locked host memory to the device, the
+    fused ply runs, and reward, done and the next proposed action cross back
+    into page-locked host memory; the host takes the proposals as its next
+    actions, so a game's ply waits on the host for its previous ply.
+
+    ``--e2e-api pipeline`` (default): ``StepPipeline`` with ``--e2e-groups``
+    groups; per step every group is received and re-sent in turn, so one
+    group's host round trip overlaps the other groups' plies.  ``step_host``:
+    one synchronous ``StrategoRolloutBuffer.step_host`` call per step (the
+    kernel reads / writes the page-locked memory in place).  ``serve``: uniform
+    steps through the persistent step server.  CUDA events around the loop.
+    Returns (updates/s, h2d, d2h bytes per step, api)."""
+    from ataraxos_b200 import StrategoRolloutBuffer
+    from ataraxos_b200.pipeline import StepPipeline
     from ataraxos_b200.serve import StepServer
 
-    B = buf.n_games
-    total = ctx.world * B if total_envs is None else total_envs
-    r = buf.step_host(None, policy=policy)
-    # untimed warm-up of the same host loop for about half a second (the
-    # host round trips of a process that has just started run slower)
-    h_act = torch.empty(B, dtype=torch.int64, pin_memory=True)
-    t_end, i = time.perf_counter() + 0.5, 0
-    while i < ctx.args.warmup or time.perf_counter() < t_end:
-        h_act.copy_(r.next_action)
-        r = buf.step_host(h_act, policy=policy)
-        i += 1
-    ctx.barrier()
-    torch.cuda.synchronize(ctx.dev)
+    a = ctx.args
+    api = a.e2e_api
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if ctx.args.e2e_api == "serve" and policy == "uniform" and B <= StepServer.max_envs(buf.device):
-        st = torch.cuda.Stream(ctx.dev)
-        e0.record(st)
-        with StepServer(buf, stream=st) as srv:
-            acts = srv.actions
-            acts.copy_(r.next_action)
-            for _ in range(steps):
-                r = srv.step(acts)
-                acts.copy_(r.next_action)
-        e1.record(st)
-        api = "StrategoRolloutBuffer.serve().step (persistent step server)"
-    else:
+    if api == "pipeline":
+        G = a.e2e_groups
+        p = StepPipeline(B, ctx.local, groups=G, env_base=env_base, **buf_kw)
+        p.reset_all_from_pool()
+        for g in range(G):
+            p.send(g, None, policy=policy)
+
+        def loop(k: int) -> None:
+            for _ in range(k):
+                for g in range(G):
+                    r = p.recv(g)
+                    p.send(g, r.next_action, policy=policy)
+
+        # untimed warm-up of the same host loop for about half a second (the
+        # host round trips of a process that has just started run slower)
+        t_end = time.perf_counter() + 0.5
+        while time.perf_counter() < t_end:
+            loop(a.warmup)
+        p.synchronize()
+        ctx.barrier()
+        torch.cuda.synchronize(ctx.dev)
         e0.record(ctx.stream)
-        for _ in range(steps):
+        loop(steps)
+        p.synchronize()
+        e1.record(ctx.stream)
+        for g in range(G):
+            p.recv(g)
+        name = f"ataraxos_b200.pipeline.StepPipeline ({G} groups; each group's ply one sb_step_host call)"
+    else:
+        buf = StrategoRolloutBuffer(B, ctx.local, env_base=env_base, **buf_kw)
+        buf.reset_all_from_pool()
+        r = buf.step_host(None, policy=policy)
+        h_act = torch.empty(B, dtype=torch.int64, pin_memory=True)
+        t_end, i = time.perf_counter() + 0.5, 0
+        while i < a.warmup or time.perf_counter() < t_end:
             h_act.copy_(r.next_action)
             r = buf.step_host(h_act, policy=policy)
-        e1.record(ctx.stream)
-        api = "StrategoRolloutBuffer.step_host"
+            i += 1
+        ctx.barrier()
+        torch.cuda.synchronize(ctx.dev)
+        if api == "serve" and policy == "uniform" and B <= StepServer.max_envs(buf.device):
+            st = torch.cuda.Stream(ctx.dev)
+            e0.record(st)
+            with StepServer(buf, stream=st) as srv:
+                acts = srv.actions
+                acts.copy_(r.next_action)
+                for _ in range(steps):
+                    r = srv.step(acts)
+                    acts.copy_(r.next_action)
+            e1.record(st)
+            name = "StrategoRolloutBuffer.serve().step (persistent step server)"
+        else:
+            e0.record(ctx.stream)
+            for _ in range(steps):
+                h_act.copy_(r.next_action)
+                r = buf.step_host(h_act, policy=policy)
+            e1.record(ctx.stream)
+            name = "StrategoRolloutBuffer.step_host"
     torch.cuda.synchronize(ctx.dev)
     ctx.barrier()
     ms = ctx.max_over_ranks(e0.elapsed_time(e1))
-    return total * steps / (ms / 1e3), B * 8, int(r.reward.numel() * 4 + r.next_action.numel() * 2
-                                                  + r.done.numel()), api
+    # per game and step: the int64 action in; f32 reward, i16 next action, u8 done out
+    return total * steps / (ms / 1e3), B * 8, B * (4 + 2 + 1), name
 
 
 def run_step_config(ctx: Ctx, cfg: int) -> dict:
     """Configs 2 (4096 envs/GPU, uniform) and 3 (262144 envs split over the GPUs, Gumbel-max
-    over virtual N(0,1) logits, 1M-entry pool): one fused-kernel ply per step."""
-    from ataraxos_b200 import StrategoRolloutBuffer
-
+    over virtual N(0,1) logits, 1M-entry pool): one fused-kernel ply per group per step."""
     a = ctx.args
     if cfg == 2:
         B, pool, policy, env_base = a.envs, POOL, "uniform", ctx.rank * a.envs
+        total = ctx.world * B
     else:
         total = a.envs if a.envs != 4096 else 262144
         env_base, B = sharding.shard_range(total, ctx.world, ctx.rank)
         pool, policy = 1 << 20, "gumbel"
-    buf = StrategoRolloutBuffer(B, ctx.local, seed=SEED, env_base=env_base, pool_size=pool, pool_seed=SEED,
-                                obs_dtype=torch.bfloat16, obs_layout="dense", mask_format="u8")
-    buf.reset_all_from_pool()
+    G = a.groups if a.groups else (3 if cfg == 2 else 2)
+    buf_kw = dict(seed=SEED, pool_size=pool, pool_seed=SEED, obs_dtype=torch.bfloat16, obs_layout="dense",
+                  mask_format="u8")
     graph = cfg == 2 and a.timing == "graph"
-    # config 2 under graph timing: the steps write 4 output sets in turn (see the module docstring)
-    sets = [buf._ensure_outputs()] + [buf.new_outputs() for _ in range(3)] if graph else [None]
-
-    def launch(i):
-        buf.step(None, policy=policy, outputs=sets[i % len(sets)])
-
+    if cfg == 2 and a.timing == "flush" and G != 1:
+        raise SystemExit("--timing flush times launches one by one: use --groups 1")
+    # config 2 under graph timing: each group writes 4 output sets in turn (see the module docstring)
+    groups = Groups(ctx, B, env_base, G, 4 if graph else 1, **buf_kw)
     for i in range(a.warmup):
-        launch(i)
+        groups.step(i, policy)
+    torch.cuda.synchronize(ctx.dev)
     if graph:
-        total_ms, clocks = timed_graph(ctx, launch, a.warmup, a.steps)
+        total_ms, clocks = timed_graph(ctx, groups, a.warmup, a.steps, policy)
+    elif cfg == 2 and a.timing == "flush":
+        buf, _, _ = groups.parts[0]
+        total_ms, clocks = timed_launches(ctx, lambda i: buf.step(None, policy=policy), a.steps, a.flush_mib)
     else:
-        flush = a.flush_mib if cfg == 2 else 0  # config 3 writes 6.7 GB/GPU per step: far above L2
-        total_ms, clocks = timed_launches(ctx, launch, a.steps, flush)
-    launch_ms = total_ms / a.steps
-    stats = ctx.gather_stats(buf.episode_stats().clone())
+        # config 3 writes 6.7 GB per GPU per step: far above L2, no flush
+        total_ms, clocks = timed_streams(ctx, groups, a.warmup, a.steps, policy)
+    if groups.status():
+        raise SystemExit(f"device status {groups.status():#x} after the timed steps")
+    stats = ctx.gather_stats(groups.stats())
+    del groups
+    torch.cuda.synchronize(ctx.dev)
+    torch.cuda.empty_cache()
+    step_ms = total_ms / a.steps
+    e2e_steps = a.e2e_steps if cfg == 2 else max(10, a.e2e_steps // 10)
+    e2e, h2d, d2h, api = e2e_loop(ctx, B, env_base, buf_kw, e2e_steps, policy, total)
+    split = (f"{G} groups of ~{B // G} envs, each on its own CUDA stream (their launches run concurrently)"
+             if G > 1 else "one launch per step")
     if cfg == 2:
-        e2e, h2d, d2h, api = e2e_loop(ctx, buf, a.e2e_steps)
         workload = (f"config2: {B} envs/GPU, seeded random setups (pool {pool}), uniform random legal actions, "
                     "auto-reset, bf16 [B,488,10,10] infostate (75 live planes rewritten per ply), u8 [B,100,100] "
-                    "mask; one step = one fused-kernel ply over all envs")
+                    f"mask; one step = one fused-kernel ply over all envs ({split})")
         if graph:
-            l2 = ("back-to-back steps (one CUDA graph of the K timed launches); outputs written to 4 sets in turn "
-                  "(4 x 441 MB, 14x L2): no step rewrites lines held in L2, every step's writes reach HBM in the "
-                  "timed region")
+            l2 = ("back-to-back steps (one CUDA graph of the K timed steps); each group writes 4 output sets in turn "
+                  "(4 x 441 MB in all, 14x L2): no step rewrites lines held in L2, every step's writes reach HBM in "
+                  "the timed region")
         else:
             l2 = f"flushed between timed steps ({a.flush_mib} MiB write, then {a.flush_mib // 2} MiB read)"
         scaling = "weak"
     else:
-        e2e, h2d, d2h, api = e2e_loop(ctx, buf, max(10, a.e2e_steps // 10), policy, total)
         workload = (f"config3: {total} envs split over {ctx.world} GPU(s) ({B}/GPU), actions by Gumbel-max "
                     "over virtual Philox N(0,1) logits of the legal moves (logits never materialised), setups from "
-                    f"a {pool}-entry pool, auto-reset, bf16 dense infostate + u8 mask")
+                    f"a {pool}-entry pool, auto-reset, bf16 dense infostate + u8 mask; one step = one ply of "
+                    f"every env ({split})")
         l2 = "outputs of one step (25.5 KB/env) exceed L2 many times; no flush"
         scaling = "strong"
     return {
-        "value": (ctx.world * B if cfg == 2 else total) * a.steps / (total_ms / 1e3), "ms_per_step": launch_ms,
-        "launch_ms": launch_ms,
+        "value": (ctx.world * B if cfg == 2 else total) * a.steps / (total_ms / 1e3), "ms_per_step": step_ms,
+        "launch_ms": step_ms,
         "envs_per_launch": B, "plies_per_launch": 1, "bytes_per_update": BYTES_PER_UPDATE, "clocks": clocks,
         "stats": stats, "e2e": {"value": e2e, "unit": "updates/s", "h2d_bytes_per_step": h2d,
                                 "d2h_bytes_per_step": d2h, "api": api},
-        "gpu_launches": a.steps, "config": {"workload": workload, "envs_per_gpu": B, "l2": l2,
-                                            "parallelism": f"env-sharded x{ctx.world}, no step-path collective"},
+        "gpu_launches": a.steps * G, "config": {"workload": workload, "envs_per_gpu": B, "groups": G, "l2": l2,
+                                                "parallelism": f"env-sharded x{ctx.world}, no step-path collective"},
         "scaling": scaling,
+        "kernel": ("env_kernel (fused step)" if G == 1 else
+                   f"env_kernel (fused step), {G} concurrent launches per step (one per group): achieved = the "
+                   "step's algorithmic bytes / the step's time"),
         "traffic": _profile_traffic("step_kernel_config2.txt") if cfg == 2 else _profile_traffic("step_kernel_config3.txt", B),
     }
 
@@ -498,106 +652,213 @@ def run_step_config(ctx: Ctx, cfg: int) -> dict:
 def run_traj_config(ctx: Ctx) -> dict:
     """Config 4: 32768 envs/GPU, T=128 ring of compact bf16 infostate, bit-packed masks,
     int16 actions, f32 log-probs (Gumbel over virtual N(0,1) logits), f32 rewards, u8 dones.
-    One timed launch = `plies_per_launch` plies with every record kept on chip."""
+    One step = `plies_per_launch` plies of every env: one launch per group (the
+    GPU's envs as ``--groups`` buffers, each with its own ring and stream, the
+    launches running concurrently), every record kept on chip in the launch."""
     from ataraxos_b200 import StrategoRolloutBuffer
     from ataraxos_b200.trajectory import TrajectoryBuffer
 
     a = ctx.args
     B = a.envs if a.envs != 4096 else 32768
     T, R = a.ring_slots, a.plies_per_launch
+    G = a.groups if a.groups else 2
     if T <= R:
         raise SystemExit("--ring-slots must exceed --plies-per-launch")
-    buf = StrategoRolloutBuffer(B, ctx.local, seed=SEED, env_base=ctx.rank * B, pool_size=POOL, pool_seed=SEED)
-    buf.reset_all_from_pool()
-    tr = TrajectoryBuffer(buf, T, policy="gumbel")
-    tr.prime()
+    if not 1 <= G <= B:
+        raise SystemExit(f"--groups must be in 1..{B}")
+    parts = []
+    for g in range(G):
+        off, n = sharding.shard_range(B, G, g)
+        s = torch.cuda.Stream(ctx.dev)
+        with torch.cuda.stream(s):
+            buf = StrategoRolloutBuffer(n, ctx.local, seed=SEED, env_base=ctx.rank * B + off, pool_size=POOL,
+                                        pool_seed=SEED)
+            buf.reset_all_from_pool()
+            tr = TrajectoryBuffer(buf, T, policy="gumbel")
+            tr.prime()
+        parts.append((tr, s, off, n))
+
+    def step() -> None:
+        for tr, s, _, _ in parts:
+            with torch.cuda.stream(s):
+                tr.rollout(R)
+
     for _ in range(a.warmup):
-        tr.rollout(R)
-    total_ms, clocks = timed_launches(ctx, lambda i: tr.rollout(R), a.steps, 0)
-    stats = ctx.gather_stats(tr.stats.clone())
-    # e2e: each launch is followed by a device->host read of the last ply's rewards and dones
+        step()
+    torch.cuda.synchronize(ctx.dev)
+    main = torch.cuda.Stream(ctx.dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def fork() -> None:
+        ev = torch.cuda.Event()
+        ev.record(main)
+        for _, s, _, _ in parts:
+            s.wait_event(ev)
+
+    def join() -> None:
+        for _, s, _, _ in parts:
+            ev = torch.cuda.Event()
+            ev.record(s)
+            main.wait_event(ev)
+
+    ctx.barrier()
+    torch.cuda.synchronize(ctx.dev)
+    torch.cuda.nvtx.range_push("timed")
+    with ClockSampler(ctx.dev) as clocks:
+        e0.record(main)
+        fork()
+        for _ in range(a.steps):
+            step()
+        join()
+        e1.record(main)
+        torch.cuda.synchronize(ctx.dev)
+        ctx.barrier()
+    torch.cuda.nvtx.range_pop()
+    total_ms = ctx.max_over_ranks(e0.elapsed_time(e1))
+    stats = ctx.gather_stats(sum(tr.stats.clone() for tr, _, _, _ in parts))
+    # e2e: each step (every group's launch) is followed by a device->host read of
+    # the last ply's rewards and dones of every env, then the host waits for them
     h_rew = torch.empty(B, dtype=torch.float32, pin_memory=True)
     h_done = torch.empty(B, dtype=torch.uint8, pin_memory=True)
     steps = max(5, a.steps // 4)
     ctx.barrier()
     torch.cuda.synchronize(ctx.dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(ctx.stream)
+    e0.record(main)
+    fork()
     for _ in range(steps):
-        tr.rollout(R)
-        last = (tr.slot - 1) % T
-        h_rew.copy_(tr.reward[last], non_blocking=True)
-        h_done.copy_(tr.done[last], non_blocking=True)
-        ctx.stream.synchronize()
-    e1.record(ctx.stream)
+        for tr, s, off, n in parts:
+            with torch.cuda.stream(s):
+                tr.rollout(R)
+                last = (tr.slot - 1) % T
+                h_rew[off:off + n].copy_(tr.reward[last], non_blocking=True)
+                h_done[off:off + n].copy_(tr.done[last], non_blocking=True)
+        for _, s, _, _ in parts:
+            s.synchronize()
+    join()
+    e1.record(main)
     torch.cuda.synchronize(ctx.dev)
     e2e_ms = ctx.max_over_ranks(e0.elapsed_time(e1))
     bpu = 15_000 + 1_250 + 2 + 4 + 4 + 1 + 512 / R
+    split = (f"{G} groups of ~{B // G} envs, each with its own ring and CUDA stream (their launches run "
+             "concurrently)" if G > 1 else "one launch per step")
     return {
         "value": ctx.world * B * R * a.steps / (total_ms / 1e3), "ms_per_step": total_ms / a.steps,
         "launch_ms": total_ms / a.steps, "envs_per_launch": B, "plies_per_launch": R, "bytes_per_update": bpu,
-        "clocks": clocks, "stats": stats,
+        "clocks": clocks.summary(), "stats": stats,
         "e2e": {"value": ctx.world * B * R * steps / (e2e_ms / 1e3), "unit": "updates/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": B * 5},
-        "gpu_launches": a.steps,
+        "gpu_launches": a.steps * G,
         "config": {"workload": f"config4: {B} envs/GPU, T={T} ring (compact bf16 [76,10,10] infostate, bit-packed "
                                f"mask, i16 action, f32 log-prob from virtual N(0,1) logits, f32 reward, u8 done); "
-                               f"{R} plies per launch", "envs_per_gpu": B,
+                               f"one step = {R} plies of every env ({split})", "envs_per_gpu": B, "groups": G,
                    "l2": f"ring of {T} slots ({T * B * 16.5 / 1e9:.0f} GB) far above L2; no flush",
                    "parallelism": f"env-sharded x{ctx.world}, no step-path collective"},
         "scaling": "weak", "traffic": _profile_traffic("rollout_kernel_config4.txt", B * R),
+        "kernel": ("env_kernel (rollout)" if G == 1 else
+                   f"env_kernel (rollout), {G} concurrent launches per step (one per group): achieved = the "
+                   "step's algorithmic bytes / the step's time"),
     }
 
 
 def run_search_config(ctx: Ctx) -> dict:
     """Config 5: 64 roots/GPU advanced 150 random plies, 1000 belief samples each
     (64,000 envs), 40-ply rollouts in one launch; bit-packed legal masks per ply
-    and terminal values per rollout."""
+    and terminal values per rollout.  The roots form ``--groups`` groups, each
+    with its own sample buffer and CUDA stream (their launches run
+    concurrently); one step = resample + prime + rollout of every group."""
     from ataraxos_b200 import StrategoRolloutBuffer
     from ataraxos_b200.trajectory import BeliefRollouts
 
     a = ctx.args
     n_roots, k, depth = 64, a.samples, 40
-    roots = StrategoRolloutBuffer(n_roots, ctx.local, seed=SEED, env_base=ctx.rank * n_roots, pool_size=POOL,
-                                  pool_seed=SEED)
-    roots.reset_all_from_pool()
-    for _ in range(150):
-        roots.step(None)
-    br = BeliefRollouts(roots, k, depth, seed=SEED + 1 + ctx.rank, policy="uniform")
-    br.samples.env_base = ctx.rank * n_roots * k
-    br.samples._st = br.samples._make_state()
+    G = a.groups if a.groups else 2
+    if not 1 <= G <= n_roots:
+        raise SystemExit(f"--groups must be in 1..{n_roots}")
+    parts = []
+    for g in range(G):
+        off, nr = sharding.shard_range(n_roots, G, g)
+        s = torch.cuda.Stream(ctx.dev)
+        with torch.cuda.stream(s):
+            roots = StrategoRolloutBuffer(nr, ctx.local, seed=SEED, env_base=ctx.rank * n_roots + off,
+                                          pool_size=POOL, pool_seed=SEED)
+            roots.reset_all_from_pool()
+            for _ in range(150):
+                roots.step(None)
+            br = BeliefRollouts(roots, k, depth, seed=SEED + 1 + ctx.rank, policy="uniform")
+            br.samples.env_base = (ctx.rank * n_roots + off) * k
+            br.samples._st = br.samples._make_state()
+        parts.append((br, s, off * k, nr * k))
+
+    def step(outs=None) -> None:
+        for br, s, _, _ in parts:
+            with torch.cuda.stream(s):
+                o = br.run()
+                if outs is not None:
+                    outs.append(o)
+
     for _ in range(a.warmup):
-        br.run()
+        step()
+    torch.cuda.synchronize(ctx.dev)
+    main = torch.cuda.Stream(ctx.dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
-    def one(i):
-        br.run()
+    def fork() -> None:
+        ev = torch.cuda.Event()
+        ev.record(main)
+        for _, s, _, _ in parts:
+            s.wait_event(ev)
 
-    total_ms, clocks = timed_launches(ctx, one, a.steps, 0)
+    def join() -> None:
+        for _, s, _, _ in parts:
+            ev = torch.cuda.Event()
+            ev.record(s)
+            main.wait_event(ev)
+
+    ctx.barrier()
+    torch.cuda.synchronize(ctx.dev)
+    torch.cuda.nvtx.range_push("timed")
+    with ClockSampler(ctx.dev) as clocks:
+        e0.record(main)
+        fork()
+        for _ in range(a.steps):
+            step()
+        join()
+        e1.record(main)
+        torch.cuda.synchronize(ctx.dev)
+        ctx.barrier()
+    torch.cuda.nvtx.range_pop()
+    total_ms = ctx.max_over_ranks(e0.elapsed_time(e1))
     n = n_roots * k
     h_val = torch.empty(n, dtype=torch.float32, pin_memory=True)
     steps = max(3, a.steps // 4)
     ctx.barrier()
     torch.cuda.synchronize(ctx.dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(ctx.stream)
+    e0.record(main)
+    fork()
     for _ in range(steps):
-        out = br.run()
-        h_val.copy_(out["terminal_value"], non_blocking=True)
-        ctx.stream.synchronize()
-    e1.record(ctx.stream)
+        for br, s, off, m in parts:
+            with torch.cuda.stream(s):
+                out = br.run()
+                h_val[off:off + m].copy_(out["terminal_value"], non_blocking=True)
+        for _, s, _, _ in parts:
+            s.synchronize()
+    join()
+    e1.record(main)
     torch.cuda.synchronize(ctx.dev)
     e2e_ms = ctx.max_over_ranks(e0.elapsed_time(e1))
+    split = (f"{G} groups of ~{n_roots // G} roots, each with its own samples and CUDA stream (their launches run "
+             "concurrently)" if G > 1 else "one launch of each kernel per step")
     return {
         "value": ctx.world * n * depth * a.steps / (total_ms / 1e3), "ms_per_step": total_ms / a.steps,
         "launch_ms": total_ms / a.steps, "envs_per_launch": n, "plies_per_launch": depth,
-        "bytes_per_update": 1250 + 2 + 4 + 4 + 1 + 512 / depth, "clocks": clocks,
+        "bytes_per_update": 1250 + 2 + 4 + 4 + 1 + 512 / depth, "clocks": clocks.summary(),
         "stats": [0, 0, 0, 0, 0],
         "e2e": {"value": ctx.world * n * depth * steps / (e2e_ms / 1e3), "unit": "updates/s",
                 "h2d_bytes_per_step": 0, "d2h_bytes_per_step": n * 4},
-        "gpu_launches": 3 * a.steps,
+        "gpu_launches": 3 * a.steps * G,
         "config": {"workload": f"config5: {n_roots} roots/GPU (seeded setups + 150 random plies) x {k} belief samples, "
                                f"{depth}-ply uniform rollouts in one launch; per-ply bit-packed masks, terminal values; "
-                               "one step = resample + prime + rollout", "envs_per_gpu": n,
+                               f"one step = resample + prime + rollout ({split})", "envs_per_gpu": n, "groups": G,
                    "l2": "n/a: per-launch outputs 3.2 GB/GPU", "parallelism": f"root-sharded x{ctx.world}"},
         "scaling": "weak", "traffic": _profile_traffic("search_kernels_config5.txt", n * depth),
     }
@@ -615,8 +876,13 @@ def main() -> None:
     ap.add_argument("--ring-slots", type=int, default=128, help="config 4 ring length T (smaller: profiling cases)")
     ap.add_argument("--samples", type=int, default=1000, help="config 5 belief samples per root")
     ap.add_argument("--e2e-steps", type=int, default=500)
-    ap.add_argument("--e2e-api", choices=["serve", "step_host"], default="step_host",
-                    help="host API of the e2e loop: the persistent step server or step_host")
+    ap.add_argument("--e2e-api", choices=["pipeline", "serve", "step_host"], default="pipeline",
+                    help="host API of the e2e loop: groups stepped in turn (StepPipeline), the persistent step "
+                         "server, or one synchronous step_host call per step")
+    ap.add_argument("--e2e-groups", type=int, default=2, help="groups of the e2e pipeline")
+    ap.add_argument("--groups", type=int, default=0,
+                    help="the GPU's envs (config 5: roots) as this many concurrently stepped groups, one CUDA "
+                         "stream each (0: 3 for config 2, 2 for configs 3-5)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--flush-mib", type=int, default=512)
     ap.add_argument("--timing", choices=["graph", "flush"], default="graph",
@@ -668,7 +934,7 @@ def main() -> None:
                 "traffic": r["traffic"],
                 "bytes_per_update": r["bytes_per_update"],
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
-                "kernel": "env_kernel (fused step)",
+                "kernel": r.get("kernel", "env_kernel (fused step)"),
             },
             "e2e": r["e2e"],
             "gpu_launches": r["gpu_launches"],

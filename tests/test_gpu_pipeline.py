@@ -1,0 +1,86 @@
+"""``StepPipeline`` on the B200: games split into asynchronously stepped
+groups play exactly as one buffer of all the games.
+
+* a host loop that receives, acts on and re-sends each group in turn gives,
+  per ply and per game, the reward / done / next action and the final state
+  of ``step_host`` on one buffer (random streams are keyed by the global env
+  index, so the split is invisible), for 1, 2, 3 and 5 groups and ragged
+  group sizes;
+* host actions (some illegal: ignored and counted) and device proposals mix;
+* misuse (a second send before recv, recv with nothing in flight, more groups
+  than games) is refused.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from _helpers import assert_state_equal, export_np
+
+pytestmark = pytest.mark.gpu
+
+
+def _pool(seed):
+    return torch.from_numpy(oracle.make_setup_pool(seed, 512))
+
+
+@pytest.mark.parametrize("n,groups", [(1000, 1), (1000, 2), (1001, 3), (4096, 5)])
+def test_groups_equal_one_buffer(n, groups):
+    from ataraxos_b200 import StrategoRolloutBuffer
+    from ataraxos_b200.pipeline import StepPipeline
+
+    seed, pool = 7, _pool(7)
+    one = StrategoRolloutBuffer(n, 0, seed=seed, setup_pool=pool, no_attack_limit=40)
+    one.reset_all_from_pool()
+    p = StepPipeline(n, 0, groups=groups, seed=seed, setup_pool=pool, no_attack_limit=40)
+    p.reset_all_from_pool()
+    assert sum(m for _, m in p.ranges) == n
+    ref = one.step_host(None)
+    acts = ref.next_action.to(torch.int64)
+    for g in range(groups):
+        p.send(g, None)
+    for t in range(50):
+        for g, (off, m) in enumerate(p.ranges):
+            r = p.recv(g)
+            sl = slice(off, off + m)
+            np.testing.assert_array_equal(r.reward.numpy(), ref.reward.numpy()[sl], err_msg=f"ply {t} group {g}")
+            np.testing.assert_array_equal(r.done.numpy(), ref.done.numpy()[sl], err_msg=f"ply {t} group {g}")
+            np.testing.assert_array_equal(r.next_action.numpy(), ref.next_action.numpy()[sl],
+                                          err_msg=f"ply {t} group {g}")
+            nxt = acts[sl].clone()
+            if t % 9 == 4:
+                nxt[::6] = 0  # illegal for those games: ignored and counted
+            p.send(g, None if t % 11 == 10 else nxt)
+        x = torch.cat([p.actions[g] for g in range(groups)])
+        if t % 11 == 10:
+            ref = one.step_host(None)
+        else:
+            ref = one.step_host(x.contiguous())
+        acts = ref.next_action.to(torch.int64)
+    for g in range(groups):
+        p.recv(g)
+    p.synchronize()
+    whole = export_np(one)
+    for g, (off, m) in enumerate(p.ranges):
+        part = export_np(p.buffers[g])
+        assert_state_equal(part, {k: v[off:off + m] for k, v in whole.items()}, f"group {g}")
+        assert p.buffers[g].status() == 0
+
+
+def test_pipeline_refuses_misuse():
+    from ataraxos_b200.pipeline import StepPipeline
+
+    with pytest.raises(RuntimeError):
+        StepPipeline(2, 0, groups=3, seed=1, setup_pool=_pool(1))
+    p = StepPipeline(64, 0, groups=2, seed=1, setup_pool=_pool(1))
+    p.reset_all_from_pool()
+    with pytest.raises(RuntimeError):
+        p.recv(0)
+    p.send(0, None)
+    with pytest.raises(RuntimeError):
+        p.send(0, None)
+    p.recv(0)
+    p.synchronize()
