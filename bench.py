@@ -294,13 +294,14 @@ def run_reference_cuda(args, rank: int) -> None:
 
 
 def _profile_traffic(name: str, updates_per_launch: int | None = None) -> float | None:
-    """DRAM bytes (read + write) per launch from the ncu capture summarised in
-    profiles/<name>: its dram_bytes_per_launch, or, for a capture taken on a
-    smaller case, its dram_bytes_per_update times the updates of this launch."""
+    """DRAM bytes (read + write) per step from the ncu capture summarised in
+    profiles/<name>: its dram_bytes_per_step (config 2: the step's launches,
+    one per group), or, for a capture taken on a smaller case, its
+    dram_bytes_per_update times the updates of the step."""
     f = ROOT / "profiles" / name
     try:
         for line in f.read_text().splitlines():
-            if line.startswith("dram_bytes_per_launch:") and updates_per_launch is None:
+            if line.startswith("dram_bytes_per_step:") and updates_per_launch is None:
                 return float(line.split(":", 1)[1].split()[0])
             if line.startswith("dram_bytes_per_update:") and updates_per_launch is not None:
                 return float(line.split(":", 1)[1].split()[0]) * updates_per_launch

@@ -19,7 +19,7 @@ def _bench():
     return mod
 
 
-def test_config2_traffic_is_per_launch():
+def test_config2_traffic_is_per_step():
     t = _bench()._profile_traffic("step_kernel_config2.txt")
     assert t is not None and 30e6 < t < 110e6  # 4096 envs x 25.5 KB at most
 
