@@ -45,9 +45,9 @@ NSQ, NACT, NCH, NRING, NHIST = 100, 10000, 488, 64, 32
 
 
 def reference_root() -> Path | None:
-    """The reference checkout (``ATARAXOS_REFERENCE``, else the path this
-    build's container mounts it at), or None when absent."""
-    for cand in (os.environ.get("ATARAXOS_REFERENCE"), "/root/reference"):
+    """The reference checkout (``ATARAXOS_REFERENCE``, else a checkout named
+    ``reference`` beside this repository), or None when absent."""
+    for cand in (os.environ.get("ATARAXOS_REFERENCE"), HERE.parent.parent / "reference"):
         if cand and (Path(cand) / "csrc" / "stratego_buffer.cu").exists():
             return Path(cand)
     return None
