@@ -14,9 +14,10 @@ the GPU busy with the other groups' plies meanwhile.
 
 Every random stream is keyed by the global env index, so a game plays out
 exactly as it does in one buffer of all the games, whatever the number of
-groups.  Each group's ply is one ``sb_step_host`` call (actions read from
-page-locked host memory, reward / done / next action written into page-locked
-memory), so the data crossing PCIe per ply is that of ``step_host``.
+groups.  Each group's ply is one ``sb_step_host`` call on prebuilt arguments
+(actions read in place from the pipeline's page-locked staging, reward / done /
+next action written by the kernel into the group buffer's page-locked result
+block), so the data crossing PCIe per ply is that of ``step_host``.
 
 This is the host loop of ``SelfPlayGenerator.generate_games``
 (stratego/training/selfplay.py:190-268) with its games split into groups that
@@ -25,8 +26,11 @@ the policy serves in turn.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
+from . import _capi as C
 from . import sharding
 from .buffer import HostStepOutput, StrategoRolloutBuffer
 
@@ -51,6 +55,23 @@ class StepPipeline:
         # page-locked int64 action staging, one per group (read in place by the kernel)
         self.actions = [torch.zeros(max(n, 1), dtype=torch.int64, pin_memory=True)[:n] for _, n in self.ranges]
         self._pending = [None] * groups
+        # per (group, policy, host actions?): the prebuilt arguments of its
+        # sb_step_host call (the pipeline's own io blocks, the buffer's mapped
+        # result block), so a send is one native call
+        self._fast: dict = {}
+
+    def _fast_call(self, g: int, policy: str, host_actions: bool):
+        key = (g, policy, host_actions)
+        c = self._fast.get(key)
+        if c is None:
+            b = self.buffers[g]
+            h = b._host_io()
+            io = C.SbHostIo(actions_host=self.actions[g].data_ptr() if host_actions else None, actions_dev=None,
+                            back_dev=None, back_host=None, back_bytes=0, sync=0, reserved=0)
+            pol = b._policy(policy, None)
+            c = self._fast[key] = (h["fn"], h["st"], io, ctypes.byref(io), pol, ctypes.byref(pol),
+                                   h["out"]["mapped"][True], self.streams[g].cuda_stream, h["ret"]["mapped"][True])
+        return c
 
     @property
     def groups(self) -> int:
@@ -73,9 +94,24 @@ class StepPipeline:
         if actions is not None:
             a = self.actions[g]
             if actions.data_ptr() != a.data_ptr():
+                if actions.shape != a.shape:
+                    raise RuntimeError(f"group {g} takes actions of shape {tuple(a.shape)}")
                 a.copy_(actions)
-        self._pending[g] = self.buffers[g].step_host(a, policy=policy, auto_reset=auto_reset, observe=observe,
-                                                     sync=False, stream=self.streams[g])
+        b = self.buffers[g]
+        if not (auto_reset and observe) or b.n_games == 0:
+            self._pending[g] = b.step_host(a, policy=policy, auto_reset=auto_reset, observe=observe, sync=False,
+                                           stream=self.streams[g])
+            return
+        fn, st, _, io, _, pol, out, stream, ret = self._fast_call(g, policy, a is not None)
+        if torch.cuda.current_device() != self.device.index:
+            with torch.cuda.device(self.device):
+                rc = fn(st, io, b._ply, pol, 1, out, stream)
+        else:
+            rc = fn(st, io, b._ply, pol, 1, out, stream)
+        if rc:
+            C.check(rc)
+        b._ply += 1
+        self._pending[g] = ret
 
     def recv(self, g: int) -> HostStepOutput:
         """Wait for group ``g``'s ply in flight and return its results (valid

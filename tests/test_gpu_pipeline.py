@@ -7,8 +7,8 @@ groups play exactly as one buffer of all the games.
   index, so the split is invisible), for 1, 2, 3 and 5 groups and ragged
   group sizes;
 * host actions (some illegal: ignored and counted) and device proposals mix;
-* misuse (a second send before recv, recv with nothing in flight, more groups
-  than games) is refused.
+* misuse (a second send before recv, recv with nothing in flight, actions of
+  the wrong shape, more groups than games) is refused.
 """
 
 from __future__ import annotations
@@ -82,5 +82,7 @@ def test_pipeline_refuses_misuse():
     p.send(0, None)
     with pytest.raises(RuntimeError):
         p.send(0, None)
+    with pytest.raises(RuntimeError):
+        p.send(1, torch.zeros(5, dtype=torch.int64))  # group 1 holds 32 games
     p.recv(0)
     p.synchronize()
