@@ -5,7 +5,7 @@ groups play exactly as one buffer of all the games.
   per ply and per game, the reward / done / next action and the final state
   of ``step_host`` on one buffer (random streams are keyed by the global env
   index, so the split is invisible), for 1, 2, 3 and 5 groups and ragged
-  group sizes;
+  group sizes, with uniform and Gumbel-max (virtual logits) sampling;
 * host actions (some illegal: ignored and counted) and device proposals mix;
 * misuse (a second send before recv, recv with nothing in flight, actions of
   the wrong shape, more groups than games) is refused.
@@ -27,8 +27,9 @@ def _pool(seed):
     return torch.from_numpy(oracle.make_setup_pool(seed, 512))
 
 
-@pytest.mark.parametrize("n,groups", [(1000, 1), (1000, 2), (1001, 3), (4096, 5)])
-def test_groups_equal_one_buffer(n, groups):
+@pytest.mark.parametrize("n,groups,policy", [(1000, 1, "uniform"), (1000, 2, "uniform"), (1001, 3, "uniform"),
+                                             (4096, 5, "uniform"), (1001, 3, "gumbel")])
+def test_groups_equal_one_buffer(n, groups, policy):
     from ataraxos_b200 import StrategoRolloutBuffer
     from ataraxos_b200.pipeline import StepPipeline
 
@@ -38,10 +39,10 @@ def test_groups_equal_one_buffer(n, groups):
     p = StepPipeline(n, 0, groups=groups, seed=seed, setup_pool=pool, no_attack_limit=40)
     p.reset_all_from_pool()
     assert sum(m for _, m in p.ranges) == n
-    ref = one.step_host(None)
+    ref = one.step_host(None, policy=policy)
     acts = ref.next_action.to(torch.int64)
     for g in range(groups):
-        p.send(g, None)
+        p.send(g, None, policy=policy)
     for t in range(50):
         for g, (off, m) in enumerate(p.ranges):
             r = p.recv(g)
@@ -53,12 +54,12 @@ def test_groups_equal_one_buffer(n, groups):
             nxt = acts[sl].clone()
             if t % 9 == 4:
                 nxt[::6] = 0  # illegal for those games: ignored and counted
-            p.send(g, None if t % 11 == 10 else nxt)
+            p.send(g, None if t % 11 == 10 else nxt, policy=policy)
         x = torch.cat([p.actions[g] for g in range(groups)])
         if t % 11 == 10:
-            ref = one.step_host(None)
+            ref = one.step_host(None, policy=policy)
         else:
-            ref = one.step_host(x.contiguous())
+            ref = one.step_host(x.contiguous(), policy=policy)
         acts = ref.next_action.to(torch.int64)
     for g in range(groups):
         p.recv(g)
