@@ -98,10 +98,11 @@ class StepPipeline:
                     raise RuntimeError(f"group {g} takes actions of shape {tuple(a.shape)}")
                 a.copy_(actions)
         b = self.buffers[g]
-        if not (auto_reset and observe) or b.n_games == 0:
+        if not (auto_reset and observe):
             self._pending[g] = b.step_host(a, policy=policy, auto_reset=auto_reset, observe=observe, sync=False,
                                            stream=self.streams[g])
             return
+        # (the io block and the policy ride along in the tuple to stay alive)
         fn, st, _, io, _, pol, out, stream, ret = self._fast_call(g, policy, a is not None)
         if torch.cuda.current_device() != self.device.index:
             with torch.cuda.device(self.device):
