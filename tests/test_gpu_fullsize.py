@@ -8,7 +8,8 @@ restatement of the reference simulator) bit for bit:
   (uniform actions, auto-reset from a 65,536-entry pool, bf16 dense
   infostate, u8 mask), 1000 plies; every ply's action / log-prob / reward /
   done, and every 100 plies the full state, hashes, masks and infostate of
-  every game;
+  every game; and the same 4096 games as the bench steps them, in 3 groups
+  on their own streams inside CUDA graphs, 300 plies;
 * config 3: 262,144 games on one GPU, Gumbel-max over virtual N(0,1)
   logits, a 1M-entry pool, 200 plies; a subsample of 4,096 games spread over
   the whole batch is replayed with its global indices, checked every ply
@@ -114,6 +115,66 @@ def test_config2_as_benched_matches_oracle_1000_plies():
     st = buf.episode_stats().cpu().numpy()
     assert st[0] == finished and finished > 1000, (st, finished)
     assert buf.status() == 0
+
+
+def test_config2_grouped_graph_as_benched_matches_oracle():
+    """Config 2 the way bench.py times it: the 4096 games as 3 buffers over
+    contiguous global env ranges, each stepped on its own stream and writing
+    4 output sets in turn, the steps captured in one CUDA graph per 100 plies
+    (the groups' launches run concurrently); after every 100 plies the full
+    state, hashes, u8 masks and infostate bits of every game equal the
+    oracle's one run of all 4096 games."""
+    from ataraxos_b200 import sharding
+
+    B, G, plies, chunk = 4096, 3, 300, 100
+    main = torch.cuda.Stream()
+    parts = []
+    for g in range(G):
+        off, n = sharding.shard_range(B, G, g)
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            b = _buf(n, seed=SEED, env_base=off, pool_size=65536, pool_seed=SEED, obs_dtype=torch.bfloat16,
+                     obs_layout="dense", mask_format="u8")
+            b.reset_all_from_pool()
+            sets = [b._ensure_outputs()] + [b.new_outputs() for _ in range(3)]
+        parts.append((b, s, sets, off, n))
+    torch.cuda.synchronize()
+    o = oracle.OracleState(B, seed=SEED, pool=oracle.make_setup_pool(SEED, 65536))
+    o.reset_pool(force_all=True)
+    outs = [None] * G
+    for c in range(plies // chunk):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=main):
+            fork = torch.cuda.Event()
+            fork.record(main)
+            for _, s, _, _, _ in parts:
+                s.wait_event(fork)
+            for i in range(c * chunk, (c + 1) * chunk):
+                for g, (b, s, sets, _, _) in enumerate(parts):
+                    with torch.cuda.stream(s):
+                        outs[g] = b.step(None, outputs=sets[i % 4])
+            for _, s, _, _, _ in parts:
+                join = torch.cuda.Event()
+                join.record(s)
+                main.wait_event(join)
+        with torch.cuda.stream(main):
+            graph.replay()
+        torch.cuda.synchronize()
+        del graph
+        o.run(chunk, threads=THREADS)
+        ctx = f"grouped config2 after {(c + 1) * chunk} plies"
+        ref = o.export()
+        obs = o.observe(mask_u8=True, info="dense", threads=THREADS)
+        h_ref = o.hash_board()
+        for g, (b, _, _, off, n) in enumerate(parts):
+            sl = slice(off, off + n)
+            assert_state_equal(export_np(b), {k: v[sl] for k, v in ref.items()}, f"{ctx}, group {g}")
+            np.testing.assert_array_equal(b.hash_board().cpu().numpy(), h_ref[sl], err_msg=f"{ctx}: hash")
+            np.testing.assert_array_equal(outs[g].legal_mask.view(torch.uint8).cpu().numpy(), obs["mask_u8"][sl],
+                                          err_msg=f"{ctx}, group {g}: u8 mask")
+            np.testing.assert_array_equal(_bits(outs[g].infostate), obs["info"][sl],
+                                          err_msg=f"{ctx}, group {g}: infostate")
+            assert b.status() == 0
 
 
 def _spread(n_all: int, n_sub: int) -> np.ndarray:
