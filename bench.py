@@ -424,16 +424,22 @@ def timed_graph(ctx: Ctx, groups: Groups, first: int, k: int, policy: str):
     _graph_upload(g, main)
     ctx.barrier()
     torch.cuda.synchronize(ctx.dev)
+    # for the record: the same replay bracketed by events the host records
+    # around its launch of the graph (includes the graph's launch latency)
+    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("timed")
     with ClockSampler(ctx.dev) as clocks:
         with torch.cuda.stream(main):
+            h0.record(main)
             g.replay()
+            h1.record(main)
         torch.cuda.synchronize(ctx.dev)
         ctx.barrier()
     torch.cuda.nvtx.range_pop()
     total_ms = ctx.max_over_ranks(e0.elapsed_time(e1))
+    host_ms = ctx.max_over_ranks(h0.elapsed_time(h1))
     del g
-    return total_ms, clocks.summary()
+    return total_ms, clocks.summary(), host_ms
 
 
 def timed_streams(ctx: Ctx, groups: Groups, first: int, k: int, policy: str):
@@ -597,8 +603,9 @@ def run_step_config(ctx: Ctx, cfg: int) -> dict:
     for i in range(a.warmup):
         groups.step(i, policy)
     torch.cuda.synchronize(ctx.dev)
+    host_ms = None
     if graph:
-        total_ms, clocks = timed_graph(ctx, groups, a.warmup, a.steps, policy)
+        total_ms, clocks, host_ms = timed_graph(ctx, groups, a.warmup, a.steps, policy)
     elif cfg == 2 and a.timing == "flush":
         buf, _, _ = groups.parts[0]
         total_ms, clocks = timed_launches(ctx, lambda i: buf.step(None, policy=policy), a.steps, a.flush_mib)
@@ -636,7 +643,7 @@ def run_step_config(ctx: Ctx, cfg: int) -> dict:
         scaling = "strong"
     return {
         "value": (ctx.world * B if cfg == 2 else total) * a.steps / (total_ms / 1e3), "ms_per_step": step_ms,
-        "launch_ms": step_ms,
+        "launch_ms": step_ms, "host_ms_per_step": None if host_ms is None else host_ms / a.steps,
         "envs_per_launch": B, "plies_per_launch": 1, "bytes_per_update": BYTES_PER_UPDATE, "clocks": clocks,
         "stats": stats, "e2e": {"value": e2e, "unit": "updates/s", "h2d_bytes_per_step": h2d,
                                 "d2h_bytes_per_step": d2h, "api": api},
@@ -939,9 +946,15 @@ def main() -> None:
             },
             "e2e": r["e2e"],
             "gpu_launches": r["gpu_launches"],
+            "timing": ("device span of the K steps: CUDA events recorded inside the CUDA graph, before the fork "
+                       "and after the join of the groups' chains; ms_per_step_with_graph_launch: the same replay "
+                       "bracketed by events the host records around its launch of the graph"
+                       if r.get("host_ms_per_step") is not None else "CUDA events on the host-launched stream"),
             "clocks": r["clocks"],
             "episode_stats": dict(zip(["finished", "red_wins", "blue_wins", "draws", "sum_lengths"], r["stats"])),
         }
+        if r.get("host_ms_per_step") is not None:
+            line["ms_per_step_with_graph_launch"] = r["host_ms_per_step"]
         if ctx.world == 1 and not args.no_cpu_baseline and args.config == 2:
             line["cpu_baseline"] = cpu_baseline(args.envs)
         print(json.dumps(line), flush=True)
