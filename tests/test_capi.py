@@ -86,3 +86,14 @@ def test_null_state_is_rejected(name):
     fn = getattr(C.lib(), name)
     args = [0 if t in (ctypes.c_int, ctypes.c_int64) else None for t in fn.argtypes]
     assert fn(*args) == C.SB_E_ARG
+
+
+def test_step_pipeline_refuses_bad_group_counts_before_allocating():
+    """StepPipeline checks its group count before it builds any buffer (so
+    these refusals need no GPU)."""
+    from ataraxos_b200.pipeline import StepPipeline
+
+    with pytest.raises(RuntimeError, match="groups must be >= 1"):
+        StepPipeline(64, 0, groups=0)
+    with pytest.raises(RuntimeError, match="at least one game"):
+        StepPipeline(3, 0, groups=4)
