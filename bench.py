@@ -390,16 +390,20 @@ class Groups:
         return st
 
 
-def _graph_upload(graph: torch.cuda.CUDAGraph, stream: torch.cuda.Stream) -> None:
+def _graph_upload(graph: torch.cuda.CUDAGraph, stream: torch.cuda.Stream) -> bool:
     """Upload an instantiated graph to the device before its first launch
-    (cuGraphUpload), so the timed launch does not pay for it."""
+    (cuGraphUpload), so the timed launch does not pay for it.  False (and the
+    graph is uploaded by its first launch instead) if the driver call is not
+    available or fails."""
     import ctypes
 
-    cu = ctypes.CDLL("libcuda.so.1")
-    rc = cu.cuGraphUpload(ctypes.c_void_p(graph.raw_cuda_graph_exec()), ctypes.c_void_p(stream.cuda_stream))
-    if rc != 0:
-        raise RuntimeError(f"cuGraphUpload failed: {rc}")
+    try:
+        cu = ctypes.CDLL("libcuda.so.1")
+        rc = cu.cuGraphUpload(ctypes.c_void_p(graph.raw_cuda_graph_exec()), ctypes.c_void_p(stream.cuda_stream))
+    except (OSError, AttributeError):
+        return False
     stream.synchronize()
+    return rc == 0
 
 
 def timed_graph(ctx: Ctx, groups: Groups, first: int, k: int, policy: str):
