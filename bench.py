@@ -339,6 +339,22 @@ class Ctx:
         return sharding.gather_episode_stats(stats).sum(0).tolist()
 
 
+def fork(main: torch.cuda.Stream, streams) -> None:
+    """Every stream in ``streams`` waits for the work queued on ``main`` so far."""
+    ev = torch.cuda.Event()
+    ev.record(main)
+    for s in streams:
+        s.wait_event(ev)
+
+
+def join(main: torch.cuda.Stream, streams) -> None:
+    """``main`` waits for the work queued on every stream in ``streams`` so far."""
+    for s in streams:
+        ev = torch.cuda.Event()
+        ev.record(s)
+        main.wait_event(ev)
+
+
 class Groups:
     """The rank's games as ``G`` buffers (contiguous global env ranges), each
     stepped on its own CUDA stream, so the groups' launches run concurrently:
@@ -369,16 +385,10 @@ class Groups:
                 b.step(None, policy=policy, outputs=sets[i % len(sets)])
 
     def fork(self, main: torch.cuda.Stream) -> None:
-        ev = torch.cuda.Event()
-        ev.record(main)
-        for _, s, _ in self.parts:
-            s.wait_event(ev)
+        fork(main, [s for _, s, _ in self.parts])
 
     def join(self, main: torch.cuda.Stream) -> None:
-        for _, s, _ in self.parts:
-            ev = torch.cuda.Event()
-            ev.record(s)
-            main.wait_event(ev)
+        join(main, [s for _, s, _ in self.parts])
 
     def stats(self) -> torch.Tensor:
         return sum(b.episode_stats().clone() for b, _, _ in self.parts)
@@ -700,28 +710,16 @@ def run_traj_config(ctx: Ctx) -> dict:
     torch.cuda.synchronize(ctx.dev)
     main = torch.cuda.Stream(ctx.dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-
-    def fork() -> None:
-        ev = torch.cuda.Event()
-        ev.record(main)
-        for _, s, _, _ in parts:
-            s.wait_event(ev)
-
-    def join() -> None:
-        for _, s, _, _ in parts:
-            ev = torch.cuda.Event()
-            ev.record(s)
-            main.wait_event(ev)
-
+    streams = [s for _, s, _, _ in parts]
     ctx.barrier()
     torch.cuda.synchronize(ctx.dev)
     torch.cuda.nvtx.range_push("timed")
     with ClockSampler(ctx.dev) as clocks:
         e0.record(main)
-        fork()
+        fork(main, streams)
         for _ in range(a.steps):
             step()
-        join()
+        join(main, streams)
         e1.record(main)
         torch.cuda.synchronize(ctx.dev)
         ctx.barrier()
@@ -736,7 +734,7 @@ def run_traj_config(ctx: Ctx) -> dict:
     ctx.barrier()
     torch.cuda.synchronize(ctx.dev)
     e0.record(main)
-    fork()
+    fork(main, streams)
     for _ in range(steps):
         for tr, s, off, n in parts:
             with torch.cuda.stream(s):
@@ -744,9 +742,9 @@ def run_traj_config(ctx: Ctx) -> dict:
                 last = (tr.slot - 1) % T
                 h_rew[off:off + n].copy_(tr.reward[last], non_blocking=True)
                 h_done[off:off + n].copy_(tr.done[last], non_blocking=True)
-        for _, s, _, _ in parts:
+        for s in streams:
             s.synchronize()
-    join()
+    join(main, streams)
     e1.record(main)
     torch.cuda.synchronize(ctx.dev)
     e2e_ms = ctx.max_over_ranks(e0.elapsed_time(e1))
@@ -813,28 +811,16 @@ def run_search_config(ctx: Ctx) -> dict:
     torch.cuda.synchronize(ctx.dev)
     main = torch.cuda.Stream(ctx.dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-
-    def fork() -> None:
-        ev = torch.cuda.Event()
-        ev.record(main)
-        for _, s, _, _ in parts:
-            s.wait_event(ev)
-
-    def join() -> None:
-        for _, s, _, _ in parts:
-            ev = torch.cuda.Event()
-            ev.record(s)
-            main.wait_event(ev)
-
+    streams = [s for _, s, _, _ in parts]
     ctx.barrier()
     torch.cuda.synchronize(ctx.dev)
     torch.cuda.nvtx.range_push("timed")
     with ClockSampler(ctx.dev) as clocks:
         e0.record(main)
-        fork()
+        fork(main, streams)
         for _ in range(a.steps):
             step()
-        join()
+        join(main, streams)
         e1.record(main)
         torch.cuda.synchronize(ctx.dev)
         ctx.barrier()
@@ -846,15 +832,15 @@ def run_search_config(ctx: Ctx) -> dict:
     ctx.barrier()
     torch.cuda.synchronize(ctx.dev)
     e0.record(main)
-    fork()
+    fork(main, streams)
     for _ in range(steps):
         for br, s, off, m in parts:
             with torch.cuda.stream(s):
                 out = br.run()
                 h_val[off:off + m].copy_(out["terminal_value"], non_blocking=True)
-        for _, s, _, _ in parts:
+        for s in streams:
             s.synchronize()
-    join()
+    join(main, streams)
     e1.record(main)
     torch.cuda.synchronize(ctx.dev)
     e2e_ms = ctx.max_over_ranks(e0.elapsed_time(e1))
