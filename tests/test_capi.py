@@ -97,3 +97,24 @@ def test_step_pipeline_refuses_bad_group_counts_before_allocating():
         StepPipeline(64, 0, groups=0)
     with pytest.raises(RuntimeError, match="at least one game"):
         StepPipeline(3, 0, groups=4)
+
+
+def test_c_host_compiles_and_links_against_the_header_and_library(tmp_path):
+    """A C program written only against include/stratego_b200.h
+    (tests/c_host/c_host_loop.c) compiles warning-free as C11 and links against
+    libstratego_b200.so; tests/test_gpu_c_host.py runs it on a GPU."""
+    import os
+    import shutil
+
+    gcc = shutil.which("gcc")
+    cuda = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
+    if gcc is None or not (cuda / "include" / "cuda_runtime.h").exists():
+        pytest.skip("no C compiler or CUDA runtime headers here")
+    lib_dir = Path(C.LIB_PATH).resolve().parent
+    exe = tmp_path / "c_host_loop"
+    r = subprocess.run([gcc, "-O2", "-std=c11", "-Wall", "-Wextra", "-Werror", f"-I{ROOT / 'include'}",
+                        f"-I{cuda / 'include'}", str(ROOT / "tests" / "c_host" / "c_host_loop.c"), f"-L{lib_dir}",
+                        "-lstratego_b200", f"-L{cuda / 'lib64'}", "-lcudart", f"-Wl,-rpath,{lib_dir}", "-o", str(exe)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    assert exe.exists()
